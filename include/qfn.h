@@ -1,0 +1,125 @@
+/*
+ * qfn.h -- C ABI of the B200 (sm_100a) quantized matrix-product library.
+ *
+ * Scope: the quantized matrix products of a Qwen3.8-Flash-Next-style MoE
+ * decoder.  Every entry point takes plain device pointers, sizes and a CUDA
+ * stream handle; no C++ or torch types cross this boundary.  Every entry
+ * point validates its arguments on the host and returns QFN_OK (0) or a
+ * positive QFN_ERR_* code; it never traps on the device.  Kernels are queued
+ * on `stream` and nothing blocks the host, so every entry point can be
+ * recorded into a CUDA graph (no allocation, no host synchronisation).
+ *
+ * Data formats (the reference's repacked expert block, repack_experts.py:2-3,
+ * 12-19 and qmoe.py:9-14):
+ *   one expert block = 2,764,800 bytes:
+ *     gate_w  u8[640][1280]  @ 0         two e2m1 codes per byte, low nibble = even k
+ *     up_w    u8[640][1280]  @ 819200
+ *     down_w  u8[2560][320]  @ 1638400
+ *     gate_s  e4m3[640][160] @ 2457600   one E4M3 scale per 16 consecutive k
+ *     up_s    e4m3[640][160] @ 2560000
+ *     down_s  e4m3[2560][40] @ 2662400
+ *   per-expert fp32 global scales s2[3] = (ws2_gate, ws2_up, ws2_down).
+ *   dequantized weight W[n][k] = E2M1[nibble] * e4m3(scale[n][k/16]) * ws2.
+ */
+#ifndef QFN_H
+#define QFN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t passed as an opaque pointer (0 = the legacy default stream). */
+typedef void* qfn_stream_t;
+
+/* Status codes. */
+enum {
+    QFN_OK = 0,
+    QFN_ERR_INVALID_ARG = 1,   /* null pointer, bad size, bad dtype code     */
+    QFN_ERR_ALIGNMENT = 2,     /* a pointer is not aligned as documented     */
+    QFN_ERR_CUDA = 3,          /* a CUDA runtime call failed (see message)   */
+    QFN_ERR_UNSUPPORTED = 4,   /* shape outside what the kernels implement   */
+    QFN_ERR_WORKSPACE = 5,     /* workspace too small (size query returned)  */
+    QFN_ERR_DEVICE = 6         /* device is not sm_100 / no device           */
+};
+
+/* Element type codes for `x` / `y` arguments. */
+enum { QFN_DTYPE_F32 = 0, QFN_DTYPE_BF16 = 1 };
+
+/* Model constants of the expert block (qmoe.py:9-14). */
+#define QFN_HID 2560
+#define QFN_INTER 640
+#define QFN_BLOCK_BYTES 2764800
+#define QFN_O_GW 0
+#define QFN_O_UW 819200
+#define QFN_O_DW 1638400
+#define QFN_O_GS 2457600
+#define QFN_O_US 2560000
+#define QFN_O_DS 2662400
+#define QFN_MAX_TOPK 32
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qfn_version(void);
+
+/* Static text for a status code. */
+const char* qfn_strerror(int status);
+
+/* Detail of the last failure on the calling host thread ("" if none). */
+const char* qfn_last_error(void);
+
+/*
+ * qfn_deq -- replaces qmoe.deq (qmoe.py:93-102).
+ *   out[n][k] = E2M1[nibble(w[n][k/2], k&1)] * e4m3(s[n][k/16]) * ws2   (fp32)
+ *   w: u8[N][K/2], s: u8[N][K/16] (E4M3 bytes), out: f32[N][K], all row-major
+ *   and contiguous.  K % 32 == 0.  Bit-exact with the reference.
+ */
+int qfn_deq(const uint8_t* w, const uint8_t* s, float ws2, float* out,
+            int64_t N, int64_t K, qfn_stream_t stream);
+
+/*
+ * qfn_block_deq -- replaces qmoe.block_deq (qmoe.py:105-111).
+ *   blk: one expert block (QFN_BLOCK_BYTES, 16-byte aligned) in device memory;
+ *   s2: host array of 3 floats (ws2 gate, up, down).
+ *   gate/up: f32[640][2560], down: f32[2560][640].
+ */
+int qfn_block_deq(const uint8_t* blk, const float s2[3], float* gate, float* up,
+                  float* down, qfn_stream_t stream);
+
+/*
+ * qfn_moe_decode -- replaces qmoe.moe_decode (qmoe.py:77-83), the bs=1
+ * NVFP4 SwiGLU expert layer fused over K experts plus the weighted combine:
+ *   h[j][n]  = silu(ws2_g[j] * Wg_j[n].x) * (ws2_u[j] * Wu_j[n].x)
+ *   out[r]   = sum_j coef[j] * ws2_d[j] * Wd_j[r].h[j]
+ *   table:  u8[n_blocks][QFN_BLOCK_BYTES] device, 16-byte aligned.  Either
+ *           the reference's slot table or the whole HBM-resident expert table.
+ *   sidx:   int32[K] device, block index of expert j (0 <= sidx < n_blocks;
+ *           an out-of-range index is not read: it yields NaN in `out`).
+ *   s2:     f32[K][3] device; coef: f32[K] device.
+ *   x:      [2560] device, dtype QFN_DTYPE_BF16 or QFN_DTYPE_F32.
+ *   h_buf:  f32[>=K][640] device scratch (the reference's h_buf).  On return
+ *           it holds h, as in the reference.
+ *   out:    f32[2560] device; written (not accumulated).
+ *   1 <= K <= QFN_MAX_TOPK.
+ */
+int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
+                   const float* s2, const float* coef, const void* x, int x_dtype,
+                   float* h_buf, float* out, int K, qfn_stream_t stream);
+
+/*
+ * qfn_gemv_e4m3 -- replaces fp8gemv.gemv (fp8gemv.py:20-26).
+ *   y[n] = s[n] * sum_k e4m3(q[n][k]) * x[k], fp32 accumulation.
+ *   q: u8[N][K] (float8_e4m3fn bytes) device, 16-byte aligned, K % 16 == 0.
+ *   s: f32[N] device; x: bf16[K] device (raw 16-bit words).
+ *   y: [N] device, y_dtype QFN_DTYPE_BF16 (the reference's output, rounded to
+ *      nearest even) or QFN_DTYPE_F32 (the unrounded accumulator * s).
+ */
+int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
+                  int y_dtype, int64_t N, int64_t K, qfn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QFN_H */

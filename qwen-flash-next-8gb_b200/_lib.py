@@ -1,0 +1,77 @@
+"""ctypes binding of libqfn.so, the C ABI declared in include/qfn.h.
+
+The library is loaded from this directory (built in-tree by build.py).  There
+is no fallback: if the library is missing or the device is not an sm_100
+part, every call raises.
+"""
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqfn.so")
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+# name -> (argtypes); every entry point returns int status.
+SIGNATURES = {
+    "qfn_deq": [_P, _P, ctypes.c_float, _P, _I64, _I64, _P],
+    "qfn_block_deq": [_P, _P, _P, _P, _P, _P],
+    "qfn_moe_decode": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _P],
+    "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
+}
+
+
+class QfnError(RuntimeError):
+    """A libqfn entry point returned a non-zero status."""
+
+
+_lib = None
+
+
+def lib():
+    """Load libqfn.so once (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python {HERE}/build.py` "
+                              "(or __graft_entry__.build()); there is no non-CUDA fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        L.qfn_version.restype = _I
+        L.qfn_strerror.argtypes = [_I]
+        L.qfn_strerror.restype = ctypes.c_char_p
+        L.qfn_last_error.restype = ctypes.c_char_p
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = argtypes
+            fn.restype = _I
+        _lib = L
+    return _lib
+
+
+def check(rc, what):
+    if rc != 0:
+        L = lib()
+        raise QfnError(f"{what}: {L.qfn_strerror(rc).decode()} ({L.qfn_last_error().decode()})")
+
+
+def stream_of(t):
+    """Raw cudaStream_t of torch's current stream on tensor t's device."""
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(name, t, dtype=None, contiguous=True):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (libqfn has no CPU path)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")

@@ -1,0 +1,126 @@
+// Shared device helpers for the sm_100a kernels of libqfn.
+//
+// Number formats (the reference's NVFP4 layout, qmoe.py:3,87,95-101):
+//  * e2m1: 4-bit code, bit 3 = sign, magnitudes {0,.5,1,1.5,2,3,4,6}; two codes
+//    per byte, the LOW nibble is the even k index.
+//  * e4m3 ("float8_e4m3fn"): 1-4-3, bias 7, no infinities, 0x7f/0xff = NaN.
+// Both convert exactly to f16 with the hardware cvt instructions used below.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace qfn {
+
+constexpr int kHid = 2560;
+constexpr int kInter = 640;
+constexpr int64_t kBlock = 2764800;
+constexpr int64_t kOGW = 0, kOUW = 819200, kODW = 1638400;
+constexpr int64_t kOGS = 2457600, kOUS = 2560000, kODS = 2662400;
+
+// Four e2m1 pairs (one 32-bit word = 8 codes) -> four f16x2 words.  Word i
+// holds byte i of `w`: low half = low nibble (even k), high half = high nibble.
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&o)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
+}
+
+// Four e4m3 bytes -> two f16x2 words: lo = bytes (0,1), hi = bytes (2,3); the
+// lower byte of each pair lands in the lower half.
+__device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\t"
+      "mov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
+// One e4m3 byte (low 8 bits of b) -> fp32, exact.
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 a;\n\t"
+      "cvt.u16.u32 a, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\t}"
+      : "=r"(r)
+      : "r"(b & 0xffu));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(r & 0xffffu)));
+}
+
+__device__ __forceinline__ float2 f16x2_to_f32x2(uint32_t v) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  return __half22float2(h);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) {
+  return __uint_as_float(b16 << 16);
+}
+
+// Streaming 128/64-bit loads of weights that are read exactly once: bypass L1
+// allocation so the x vector / scratch keep the cache.
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream_u8(const void* p) {
+  uint32_t v;
+  asm volatile("{\n\t.reg .u16 t;\n\t"
+               "ld.global.nc.L1::no_allocate.u8 t, [%1];\n\t"
+               "cvt.u32.u16 %0, t;\n\t}"
+               : "=r"(v)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Programmatic dependent launch controls (no-ops when the launch carries no
+// programmatic dependency).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 16 e2m1 codes (8 bytes) . 16 fp32 x values held as four float4 -> fp32 sum.
+__device__ __forceinline__ float dot16_e2m1(uint2 w, float4 x0, float4 x1, float4 x2, float4 x3) {
+  uint32_t h[8];
+  e2m1x8_to_f16x2(w.x, *reinterpret_cast<uint32_t(*)[4]>(&h[0]));
+  e2m1x8_to_f16x2(w.y, *reinterpret_cast<uint32_t(*)[4]>(&h[4]));
+  float2 a;
+  float s;
+  a = f16x2_to_f32x2(h[0]); s = a.x * x0.x;      s = fmaf(a.y, x0.y, s);
+  a = f16x2_to_f32x2(h[1]); s = fmaf(a.x, x0.z, s); s = fmaf(a.y, x0.w, s);
+  a = f16x2_to_f32x2(h[2]); s = fmaf(a.x, x1.x, s); s = fmaf(a.y, x1.y, s);
+  a = f16x2_to_f32x2(h[3]); s = fmaf(a.x, x1.z, s); s = fmaf(a.y, x1.w, s);
+  a = f16x2_to_f32x2(h[4]); s = fmaf(a.x, x2.x, s); s = fmaf(a.y, x2.y, s);
+  a = f16x2_to_f32x2(h[5]); s = fmaf(a.x, x2.z, s); s = fmaf(a.y, x2.w, s);
+  a = f16x2_to_f32x2(h[6]); s = fmaf(a.x, x3.x, s); s = fmaf(a.y, x3.y, s);
+  a = f16x2_to_f32x2(h[7]); s = fmaf(a.x, x3.z, s); s = fmaf(a.y, x3.w, s);
+  return s;
+}
+
+}  // namespace qfn

@@ -1,0 +1,39 @@
+// Host-side helpers shared by the C-ABI entry points: status/message
+// handling, per-device properties, launch checking.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/qfn.h"
+
+namespace qfn {
+
+// Record a message for qfn_last_error() on this host thread; returns status.
+int set_error(int status, const char* fmt, ...);
+
+struct DeviceInfo {
+  int device;
+  int sm_count;
+  int cc_major, cc_minor;
+  size_t smem_optin;
+};
+
+// Properties of the current device (cached per device).  Returns QFN_OK,
+// QFN_ERR_CUDA or QFN_ERR_DEVICE (not compute capability 10.x).
+int current_device(DeviceInfo** out);
+
+inline cudaStream_t as_stream(qfn_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Check the launch that was just queued.
+int check_launch(const char* what);
+
+}  // namespace qfn
+
+#define QFN_REQUIRE(cond, status, ...)                 \
+  do {                                                 \
+    if (!(cond)) return ::qfn::set_error((status), __VA_ARGS__); \
+  } while (0)

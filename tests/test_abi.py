@@ -1,0 +1,104 @@
+"""The C-ABI library loads and exports every entry point include/qfn.h
+declares; host-side argument validation returns status codes without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import _lib
+from conftest import REPO
+
+HEADERS = [os.path.join(REPO, "include", f) for f in sorted(os.listdir(os.path.join(REPO, "include")))
+           if f.endswith(".h")]
+
+
+def declared():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names |= set(re.findall(r"\b(qfn_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for must in ("qfn_moe_decode", "qfn_gemv_e4m3", "qfn_deq", "qfn_block_deq", "qfn_version",
+                 "qfn_strerror", "qfn_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_signatures_cover_compute_entry_points():
+    compute = [n for n in declared() if n not in ("qfn_version", "qfn_strerror", "qfn_last_error")]
+    assert sorted(compute) == sorted(_lib.SIGNATURES)
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.qfn_version() >= 100
+    assert lib.qfn_strerror(0) == b"ok"
+    assert lib.qfn_strerror(1) == b"invalid argument"
+    assert lib.qfn_strerror(999) == b"unknown status"
+
+
+def test_validation_rejects_bad_arguments_without_touching_a_device():
+    lib = _lib.lib()
+    # null pointers
+    assert lib.qfn_moe_decode(None, 1, None, None, None, None, 1, None, None, 10, None) == 1
+    assert lib.qfn_gemv_e4m3(None, None, None, None, 1, 16, 16, None) == 1
+    assert lib.qfn_deq(None, None, ctypes.c_float(1.0), None, 1, 32, None) == 1
+    assert b"null" in lib.qfn_last_error()
+    fake = ctypes.c_void_p(0x10000)   # never dereferenced: validation fails first
+    # K outside [1, 32]
+    assert lib.qfn_moe_decode(fake, 1, fake, fake, fake, fake, 1, fake, fake, 33, None) == 4
+    assert lib.qfn_moe_decode(fake, 1, fake, fake, fake, fake, 1, fake, fake, 0, None) == 4
+    # n_blocks must be positive; x dtype code must be known
+    assert lib.qfn_moe_decode(fake, 0, fake, fake, fake, fake, 1, fake, fake, 10, None) == 1
+    assert lib.qfn_moe_decode(fake, 1, fake, fake, fake, fake, 7, fake, fake, 10, None) == 1
+    # misaligned table
+    odd = ctypes.c_void_p(0x10001)
+    assert lib.qfn_moe_decode(odd, 1, fake, fake, fake, fake, 1, fake, fake, 10, None) == 2
+    # GEMV: K % 16, dtype, alignment
+    assert lib.qfn_gemv_e4m3(fake, fake, fake, fake, 1, 16, 24, None) == 4
+    assert lib.qfn_gemv_e4m3(fake, fake, fake, fake, 5, 16, 32, None) == 1
+    assert lib.qfn_gemv_e4m3(odd, fake, fake, fake, 1, 16, 32, None) == 2
+    # deq: K % 32
+    assert lib.qfn_deq(fake, fake, ctypes.c_float(1.0), fake, 4, 48, None) == 4
+
+
+def test_python_wrappers_reject_cpu_tensors():
+    import torch
+    import fp8gemv
+    import qmoe
+    q = torch.zeros(16, 32, dtype=torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="CUDA"):
+        fp8gemv.gemv(q, torch.ones(16), torch.zeros(32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        qmoe.moe_decode(torch.zeros(1, qmoe.BLOCK, dtype=torch.uint8), torch.zeros(1, dtype=torch.int32),
+                        torch.zeros(1, 3), torch.zeros(1), torch.zeros(2560), torch.zeros(1, 640),
+                        torch.zeros(1, 2560))
+    with pytest.raises(NotImplementedError):
+        qmoe.SWAP = True
+        try:
+            qmoe.deq(torch.zeros(2, 16, dtype=torch.uint8), torch.zeros(2, 2, dtype=torch.uint8), 1.0)
+        finally:
+            qmoe.SWAP = False
+
+
+def test_reference_constants_kept():
+    import qmoe
+    assert (qmoe.HID, qmoe.INTER, qmoe.BLOCK) == (2560, 640, 2764800)
+    assert (qmoe.O_GW, qmoe.O_UW, qmoe.O_DW, qmoe.O_GS, qmoe.O_US, qmoe.O_DS) == (
+        0, 819200, 1638400, 2457600, 2560000, 2662400)
+    assert (qmoe.KB_UP, qmoe.G_UP, qmoe.KB_DN, qmoe.G_DN) == (1280, 160, 320, 40)
+    assert qmoe.E2M1.tolist() == [0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6]
+    # the block layout adds up (repack_experts.py:12-19)
+    sizes = [819200] * 3 + [102400] * 3
+    assert sum(sizes) == qmoe.BLOCK and qmoe.BLOCK % 4096 == 0

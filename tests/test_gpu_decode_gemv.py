@@ -1,0 +1,205 @@
+"""GPU parity of the CUDA path against the reference's golden vectors and the
+CPU oracle, through the drop-in Python API (which calls the C ABI).
+
+Tolerances: the contract is max|cand - ref| <= 1e-3 * RMS(ref) for fp32
+results (TOL); fp32-accumulating kernels are expected to land far inside it,
+checked at FP32_GRADE.  bf16 outputs must equal the oracle rounded to bf16,
+except for values whose fp32 result sits within a few fp32 ulps of a bf16
+rounding boundary, which may differ by exactly one bf16 ulp.
+"""
+import numpy as np
+import pytest
+import torch
+
+import fp8gemv
+import oracle
+import qmoe
+import routing
+import synthetic
+from conftest import rel_err, sha
+from test_oracle_golden import _deq_all_inputs, decode_case
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+FP32_GRADE = 5e-5
+DEV = "cuda"
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def check_bf16(y_bf16, ref_f32):
+    got = y_bf16.float().cpu().numpy()
+    want = oracle.bf16_round(ref_f32)
+    diff = got != want
+    ulp = np.abs(want) * 2.0 ** -7
+    assert np.all(np.abs(got - want)[diff] <= ulp[diff]), "bf16 output off by more than one ulp"
+    assert diff.mean() < 0.01, f"{diff.mean():.4f} of bf16 outputs differ from bf16(oracle)"
+
+
+# ---------------------------------------------------------------- dequantization
+def test_deq_every_byte_and_scale_bit_exact(golden):
+    c = golden.cases["deq_all"]
+    wb, sb = _deq_all_inputs()
+    out = qmoe.deq(cuda(wb), cuda(sb), c["ws2"]).cpu().numpy()
+    assert sha(out) == c["sha256"]
+
+
+def test_block_deq_bit_exact(golden):
+    c = golden.cases["block_deq"]
+    blk = synthetic.make_blocks(1, seed=c["block_seed"])[0]
+    s2 = synthetic.make_s2(1, seed=c["s2_seed"], spread=True)[0]
+    g, u, d = qmoe.block_deq(cuda(blk), torch.from_numpy(s2))
+    assert sha(g.cpu().numpy()) == c["gate_sha256"]
+    assert sha(u.cpu().numpy()) == c["up_sha256"]
+    assert sha(d.cpu().numpy()) == c["down_sha256"]
+
+
+# ---------------------------------------------------------------- decode expert layer
+def run_decode(table, sidx, s2, coef, x):
+    K = len(sidx)
+    hb = torch.full((K, 640), float("nan"), device=DEV)
+    ob = torch.empty(K, 2560, device=DEV)
+    y = qmoe.moe_decode(table, cuda(np.asarray(sidx, np.int32)), cuda(np.asarray(s2, np.float32)),
+                        cuda(np.asarray(coef, np.float32)), x.to(DEV), hb, ob)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), hb.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["moe_decode_k10_bf16", "moe_decode_k3_f32"])
+def test_moe_decode_matches_reference_golden(golden, name):
+    table, sidx, s2, coef, x = decode_case(golden, name)
+    y, h = run_decode(cuda(table), sidx, s2, coef, x)
+    ref = golden.load(name + "_out")
+    assert rel_err(y, ref) <= TOL
+    assert rel_err(y, ref) <= FP32_GRADE
+    assert rel_err(h, golden.load(name + "_h")) <= FP32_GRADE
+    assert np.argmax(y) == np.argmax(ref)
+
+
+@pytest.fixture(scope="module")
+def table24():
+    blocks = synthetic.make_blocks(24, seed=7)
+    return blocks, cuda(blocks)
+
+
+@pytest.mark.parametrize("K,xdtype,seed", [(10, torch.bfloat16, 1), (10, torch.float32, 2), (1, torch.bfloat16, 3),
+                                           (7, torch.float32, 4), (32, torch.bfloat16, 5)])
+def test_moe_decode_matches_oracle(table24, K, xdtype, seed):
+    blocks, table = table24
+    rng = np.random.Generator(np.random.PCG64(100 + seed))
+    sidx = rng.choice(24, size=K, replace=K > 24).astype(np.int32)
+    s2 = synthetic.make_s2(K, seed=200 + seed, spread=True)
+    coef = rng.random(K).astype(np.float32)
+    x = synthetic.make_x(2560, seed=300 + seed, dtype=xdtype)
+    y, h = run_decode(table, sidx, s2, coef, x)
+    ref, href = oracle.moe_decode(blocks, sidx, s2, coef, x.float().numpy(), return_h=True)
+    assert rel_err(y, ref) <= FP32_GRADE
+    assert rel_err(h[:K], href) <= FP32_GRADE
+    assert np.argmax(y) == np.argmax(ref)
+
+
+def test_moe_decode_out_of_range_block_gives_nan_without_reading(table24):
+    _, table = table24
+    sidx = np.array([0, 1, 24, 3], np.int32)           # 24 == n_blocks: out of range
+    y, h = run_decode(table, sidx, synthetic.make_s2(4), np.ones(4, np.float32), synthetic.make_x(2560, 9))
+    assert np.isnan(y).all()
+    assert np.isnan(h[2]).all() and np.isfinite(h[[0, 1, 3]]).all()
+    sidx[2] = -5
+    y, _ = run_decode(table, sidx, synthetic.make_s2(4), np.ones(4, np.float32), synthetic.make_x(2560, 9))
+    assert np.isnan(y).all()
+
+
+def test_moe_decode_repeated_calls_identical(table24):
+    _, table = table24
+    args = (np.arange(10, dtype=np.int32), synthetic.make_s2(10), np.full(10, .1, np.float32),
+            synthetic.make_x(2560, 11))
+    a, _ = run_decode(table, *args)
+    b, _ = run_decode(table, *args)
+    assert np.array_equal(a, b)      # fixed reduction order: bit-reproducible
+
+
+def test_moe_decode_graph_capture(table24):
+    _, table = table24
+    K = 10
+    sidx = cuda(np.arange(K, dtype=np.int32) + 3)
+    s2 = cuda(synthetic.make_s2(K, seed=1, spread=True))
+    coef = cuda(np.linspace(0.05, 0.2, K).astype(np.float32))
+    x = synthetic.make_x(2560, 12).to(DEV)
+    hb = torch.empty(K, 640, device=DEV)
+    ob = torch.empty(K, 2560, device=DEV)
+    eager = qmoe.moe_decode(table, sidx, s2, coef, x, hb, ob).clone()
+    g = torch.cuda.CUDAGraph()
+    qmoe.moe_decode(table, sidx, s2, coef, x, hb, ob)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        y = qmoe.moe_decode(table, sidx, s2, coef, x, hb, ob)
+    x.copy_(synthetic.make_x(2560, 13).to(DEV))
+    g.replay()
+    torch.cuda.synchronize()
+    want = qmoe.moe_decode(table, sidx, s2, coef, x, hb, ob)
+    assert torch.equal(y, want) and not torch.equal(y, eager)
+
+
+# ---------------------------------------------------------------- FP8 GEMV
+def gemv_inputs(N, K, wseed, xseed):
+    w = synthetic.gemv_weights(N, K, wseed).float().numpy()
+    q, s = oracle.to_fp8_rows(w)
+    x = synthetic.make_x(K, seed=xseed)
+    return q, s, x
+
+
+@pytest.mark.parametrize("N,K", [(256, 512), (12288, 2560), (2560, 4096)])
+def test_gemv_matches_reference_golden(golden, N, K):
+    c = golden.cases[f"gemv_{N}x{K}"]
+    q, s, x = gemv_inputs(N, K, c["w_seed"], c["x_seed"])
+    qd = cuda(q).view(torch.float8_e4m3fn)
+    ref = golden.load(f"gemv_{N}x{K}_y")
+    y32 = fp8gemv.gemv_f32(qd, cuda(s), x.to(DEV)).cpu().numpy()
+    assert rel_err(y32, ref) <= FP32_GRADE
+    check_bf16(fp8gemv.gemv(qd, cuda(s), x.to(DEV)), oracle.gemv(q, s, x.float().numpy()))
+
+
+@pytest.mark.parametrize("N,K", [(13, 48), (1, 16), (10240, 2560), (6144, 2560), (2560, 6144), (33, 32768)])
+def test_gemv_matches_oracle_odd_shapes(N, K):
+    q, s, x = gemv_inputs(N, K, N + K, K)
+    qd = cuda(q).view(torch.float8_e4m3fn)
+    ref = oracle.gemv(q, s, x.float().numpy())
+    assert rel_err(fp8gemv.gemv_f32(qd, cuda(s), x.to(DEV)).cpu().numpy(), ref) <= FP32_GRADE
+    check_bf16(fp8gemv.gemv(qd, cuda(s), x.to(DEV)), ref)
+
+
+def test_gemv_graph_capture():
+    q, s, x = gemv_inputs(2560, 4096, 1, 2)
+    qd, sd, xd = cuda(q).view(torch.float8_e4m3fn), cuda(s), x.to(DEV)
+    fp8gemv.gemv(qd, sd, xd)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        y = fp8gemv.gemv(qd, sd, xd)
+    xd.copy_(synthetic.make_x(4096, 3).to(DEV))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, fp8gemv.gemv(qd, sd, xd))
+
+
+def test_gemv_accepts_engine_quantizer_output():
+    """The engine's own producer (to_fp8_rows on the device) feeds gemv unchanged (qwen_engine.py:71-82)."""
+    w = synthetic.gemv_weights(512, 2560, 5).to(DEV)
+    q, s = synthetic.to_fp8_rows(w)
+    x = synthetic.make_x(2560, 6).to(DEV)
+    y = fp8gemv.gemv(q, s.view(-1).contiguous(), x)
+    ref = oracle.gemv(q.view(torch.uint8).cpu().numpy(), s.view(-1).cpu().numpy(), x.float().cpu().numpy())
+    check_bf16(y, ref)
+
+
+# ---------------------------------------------------------------- routing on the device
+def test_route_on_device_matches_oracle():
+    logits = synthetic.zipf_logits(64, seed=77)
+    ti, tv = routing.route(cuda(logits))
+    oti, ocoef = oracle.route(logits)
+    assert np.array_equal(ti.cpu().numpy(), oti)
+    got = tv.float().cpu().numpy()
+    assert np.all(np.abs(got - ocoef) <= np.abs(ocoef) * 2.0 ** -7)
