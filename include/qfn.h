@@ -97,15 +97,37 @@ int qfn_block_deq(const uint8_t* blk, const float s2[3], float* gate, float* up,
  *   sidx:   int32[K] device, block index of expert j (0 <= sidx < n_blocks;
  *           an out-of-range index is not read: it yields NaN in `out`).
  *   s2:     f32[K][3] device; coef: f32[K] device.
- *   x:      [2560] device, dtype QFN_DTYPE_BF16 or QFN_DTYPE_F32.
+ *   x:      [2560] device, 16-byte aligned, dtype QFN_DTYPE_BF16 or QFN_DTYPE_F32.
  *   h_buf:  f32[>=K][640] device scratch (the reference's h_buf).  On return
  *           it holds h, as in the reference.
  *   out:    f32[2560] device; written (not accumulated).
  *   1 <= K <= QFN_MAX_TOPK.
+ *   K <= 10 runs the tensor-core path (two programmatically dependent
+ *   launches); larger K runs the CUDA-core path.  Results are bit-identical
+ *   between calls with the same inputs (fixed reduction order).
  */
 int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                    const float* s2, const float* coef, const void* x, int x_dtype,
                    float* h_buf, float* out, int K, qfn_stream_t stream);
+
+/*
+ * qfn_moe_decode_variant -- qfn_moe_decode with the kernel path chosen by the
+ * caller (no counterpart in the reference; for tests and measurements):
+ * variant 0 = automatic, 1 = tensor-core path (K <= 10), 2 = CUDA-core path.
+ */
+int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
+                           const float* s2, const float* coef, const void* x, int x_dtype,
+                           float* h_buf, float* out, int K, int variant,
+                           qfn_stream_t stream);
+
+/*
+ * qfn_device_status -- read (and with clear != 0, reset) the decode kernels'
+ * device status word of the current device: bit 0 = a bounded wait on a
+ * shared-memory barrier ran out (the outputs of that call are invalid).
+ * Synchronous (a device-to-host copy).  No counterpart in the reference,
+ * whose kernels have no waits.
+ */
+int qfn_device_status(unsigned int* status, int clear);
 
 /*
  * qfn_gemv_e4m3 -- replaces fp8gemv.gemv (fp8gemv.py:20-26).

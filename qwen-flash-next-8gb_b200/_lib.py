@@ -24,6 +24,8 @@ SIGNATURES = {
     "qfn_deq": [_P, _P, ctypes.c_float, _P, _I64, _I64, _P],
     "qfn_block_deq": [_P, _P, _P, _P, _P, _P],
     "qfn_moe_decode": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _P],
+    "qfn_moe_decode_variant": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _I, _P],
+    "qfn_device_status": [_P, _I],
     "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
 }
 
@@ -59,6 +61,13 @@ def check(rc, what):
     if rc != 0:
         L = lib()
         raise QfnError(f"{what}: {L.qfn_strerror(rc).decode()} ({L.qfn_last_error().decode()})")
+
+
+def device_status(clear=True):
+    """Device status word of the current device (bit 0: a kernel wait timed out)."""
+    v = ctypes.c_uint(0)
+    check(lib().qfn_device_status(ctypes.byref(v), int(clear)), "qfn_device_status")
+    return v.value
 
 
 def stream_of(t):

@@ -124,3 +124,107 @@ __device__ __forceinline__ float dot16_e2m1(uint2 w, float4 x0, float4 x1, float
 }
 
 }  // namespace qfn
+
+// ---------------------------------------------------------------- async copies / barriers
+namespace qfn {
+
+// Bound on every spin of a kernel on an mbarrier; a wait that runs out sets
+// kStatusTimeout in the device status word of the kernel's translation unit
+// and the kernel carries on (its outputs are then garbage; the host reads and
+// clears the word with qfn_device_status).
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kStatusTimeout = 1u;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// Arrive once and add `bytes` to the transaction count of the current phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity; false if it timed out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing
+// `bytes` of transactions on `bar`.  dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// D += A(16x16, f16, row) * B(16x8, f16, col), fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Two e4m3 scale bytes (low 16 bits of v: byte 0, byte 1) -> two f16x2
+// words each holding one scale in both halves.
+__device__ __forceinline__ void e4m3x2_to_bcast(uint32_t v, uint32_t& s0, uint32_t& s1) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 a;\n\t"
+      "cvt.u16.u32 a, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\t}"
+      : "=r"(r)
+      : "r"(v & 0xffffu));
+  s0 = __byte_perm(r, 0, 0x1010);
+  s1 = __byte_perm(r, 0, 0x3232);
+}
+
+// Power-of-two scale 2^e that maps max|v| into [2^14, 2^15) so that values
+// held as f16 keep 11 significant bits down to max * 2^-28 (e = 0 if max is
+// 0 or not finite).
+__device__ __forceinline__ int f16_prescale_exp(float maxabs) {
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 0;
+  int ex;
+  frexpf(maxabs, &ex);  // maxabs in [2^(ex-1), 2^ex)
+  return 15 - ex;
+}
+
+// v (fp32) -> f16 hi + f16 lo with hi + lo = v to ~22 significant bits.
+__device__ __forceinline__ void split_f16(float v, __half& hi, __half& lo) {
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
+
+}  // namespace qfn

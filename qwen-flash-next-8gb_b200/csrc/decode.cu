@@ -14,6 +14,8 @@
 //    It is launched as a programmatic dependent of gate_up: its CTAs start
 //    while gate_up runs, issue their first weight loads (the table and sidx
 //    were complete before gate_up started), then wait for gate_up's h.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "host.cuh"
 
@@ -34,7 +36,7 @@ constexpr int kDnBatch = 8;                                        // items per 
 __device__ __forceinline__ bool block_ok(int64_t b, int64_t n_blocks) { return b >= 0 && b < n_blocks; }
 
 template <bool kXF32>
-__global__ void __launch_bounds__(kGuThreads) moe_gate_up_kernel(const uint8_t* __restrict__ table,
+__global__ void __launch_bounds__(kGuThreads) moe_gate_up_generic_kernel(const uint8_t* __restrict__ table,
                                                                   int64_t n_blocks,
                                                                   const int32_t* __restrict__ sidx,
                                                                   const float* __restrict__ s2,
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(kGuThreads) moe_gate_up_kernel(const uint8_t* 
   }
 }
 
-__global__ void __launch_bounds__(kDnThreads) moe_down_kernel(const uint8_t* __restrict__ table, int64_t n_blocks,
+__global__ void __launch_bounds__(kDnThreads) moe_down_generic_kernel(const uint8_t* __restrict__ table, int64_t n_blocks,
                                                               const int32_t* __restrict__ sidx,
                                                               const float* __restrict__ s2,
                                                               const float* __restrict__ coef,
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(kDnThreads) moe_down_kernel(const uint8_t* __r
   }
 }
 
-static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+static int launch_moe_decode_generic(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
                              const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
                              cudaStream_t st) {
   DeviceInfo* dev;
@@ -195,16 +197,16 @@ static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32
   if (rc) return rc;
   const dim3 gu_grid(kInter / kGuFeatPerCta, K);
   if (x_dtype == QFN_DTYPE_F32)
-    moe_gate_up_kernel<true><<<gu_grid, kGuThreads, 0, st>>>(table, n_blocks, sidx, s2, x, h_buf);
+    moe_gate_up_generic_kernel<true><<<gu_grid, kGuThreads, 0, st>>>(table, n_blocks, sidx, s2, x, h_buf);
   else
-    moe_gate_up_kernel<false><<<gu_grid, kGuThreads, 0, st>>>(table, n_blocks, sidx, s2, x, h_buf);
-  rc = check_launch("moe_gate_up_kernel");
+    moe_gate_up_generic_kernel<false><<<gu_grid, kGuThreads, 0, st>>>(table, n_blocks, sidx, s2, x, h_buf);
+  rc = check_launch("moe_gate_up_generic_kernel");
   if (rc) return rc;
 
   const size_t smem = static_cast<size_t>(K) * kInter * sizeof(float);
   static bool attr_set[64] = {};
   if (smem > 48 * 1024 && !attr_set[dev->device]) {
-    cudaError_t e = cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(moe_down_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          QFN_MAX_TOPK * kInter * static_cast<int>(sizeof(float)));
     if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "down smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev->device] = true;
@@ -219,19 +221,478 @@ static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, moe_down_kernel, table, n_blocks, sidx, s2, coef,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, moe_down_generic_kernel, table, n_blocks, sidx, s2, coef,
                                      static_cast<const float*>(h_buf), out, K);
-  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_down_kernel launch: %s", cudaGetErrorString(e));
-  return check_launch("moe_down_kernel");
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_down_generic_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("moe_down_generic_kernel");
+}
+
+// ============================================================================
+// Persistent path (K <= kFastMaxK): one cooperative launch, one CTA per SM.
+//
+// Work: the gate/up phase has K*80 "gate tiles" (8 output features = their 8
+// gate rows + 8 up rows + 16 scale rows of one expert: four contiguous pieces,
+// 23,040 B); the down phase has 160 "down tiles" (16 output rows x all K
+// experts: 2K contiguous pieces, K*5,760 B).  Down tile d belongs to CTA
+// d % grid; gate tiles are split into contiguous ranges weighted so that
+// every CTA streams about the same number of bytes (a down tile costs K/4
+// gate tiles).  At entry the lanes of warp 0 issue one bulk TMA copy per
+// piece of every tile the CTA owns, gate tiles first, each tile completing
+// its own mbarrier: the CTA's whole share of the layer is in flight at once
+// and the down rows land while the gate/up phase computes.
+//
+// Both phases reduce 16-row x 64-byte units with mma.sync m16n8k16 (tensor
+// cores as the dot-product engine): the A operand is the e2m1 codes converted
+// to f16 and multiplied by their E4M3 block scale (<= 6 significant bits:
+// exact in f16); the B operand holds x (phase 1) or coef_j * ws2_d_j * h_j
+// (phase 2) as an f16 hi/lo pair (v * 2^e = hi + lo, one power-of-two e per
+// phase) in columns 0 and 1, so every tensor-core product is exact and the
+// fp32 sums keep ~22 bits of the activations.  Folding coef_j * ws2_d_j into
+// B lets one accumulator sum all experts: the weighted combine is part of the
+// MMA.  Per-unit partials are summed in a fixed order, so results are
+// bit-reproducible.  A grid-wide barrier (cooperative groups) separates
+// writing h from reading it.
+// ============================================================================
+
+constexpr int kFastMaxK = 10;
+constexpr int kPWarps = 20;
+constexpr int kPThreads = kPWarps * 32;              // 640
+constexpr int kMaxGateTiles = 6;
+constexpr int kMaxDownTiles = 2;
+constexpr int kTileBytes = 16 * 1280 + 2 * 1280;     // 23040: gate rows | up rows | gate scales | up scales
+constexpr int kTilesPerExpert = kInter / 8;          // 80
+constexpr int kDownTiles = kHid / 16;                // 160
+constexpr int kDnWBytes = 16 * (kInter / 2);         // 5120 per expert per down tile
+constexpr int kDnSBytes = 16 * (kInter / 16);        // 640
+constexpr int kXUnits = (kHid / 128) * 16;           // 320 16-byte units per hi (or lo) array
+constexpr int kHUnitsMax = kFastMaxK * (kInter / 128) * 16;  // 800
+
+__device__ unsigned int g_decode_status = 0;
+
+__device__ __forceinline__ void note_timeout() { atomicOr(&g_decode_status, kStatusTimeout); }
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
+  return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// Exact v * 2^e for |e| <= 252 (two power-of-two factors, each a normal float).
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+  const int a = e / 2, b = e - a;
+  return v * __int_as_float((a + 127) << 23) * __int_as_float((b + 127) << 23);
+}
+
+// Block-wide max of non-negative values (NaN-propagating); all threads get it.
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = (isnan(u) || u > v) ? u : v;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = red[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = (isnan(red[w]) || red[w] > m) ? red[w] : m;
+    red[32] = m;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// One 16-row x 64-byte unit through 8 tensor-core MMAs.
+//   ra/rb: this thread's 16 bytes of rows g and g+8; sa/sb: the two E4M3
+//   scales (groups 2t, 2t+1 of the chunk) of those rows; bq: the B operand
+//   (f16 pairs for this thread's 32 k, or zero).  Word i of the 16 bytes
+//   feeds accumulator set d[i] (four independent MMA chains).
+__device__ __forceinline__ void mma_chunk(float (&d)[4][4], uint4 ra, uint4 rb, uint32_t sa, uint32_t sb,
+                                          const uint4 (&bq)[4]) {
+  uint32_t sa0, sa1, sb0, sb1;
+  e4m3x2_to_bcast(sa, sa0, sa1);
+  e4m3x2_to_bcast(sb, sb0, sb1);
+  const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
+  const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t ha[4], hb[4];
+    e2m1x8_to_f16x2(wa[i], ha);
+    e2m1x8_to_f16x2(wb[i], hb);
+    const uint32_t sA = i < 2 ? sa0 : sa1;
+    const uint32_t sB = i < 2 ? sb0 : sb1;
+    const uint32_t a0[4] = {hmul2_u32(ha[0], sA), hmul2_u32(hb[0], sB), hmul2_u32(ha[1], sA), hmul2_u32(hb[1], sB)};
+    mma_16816(d[i], a0, bq[i].x, bq[i].y);
+    const uint32_t a1[4] = {hmul2_u32(ha[2], sA), hmul2_u32(hb[2], sB), hmul2_u32(ha[3], sA), hmul2_u32(hb[3], sB)};
+    mma_16816(d[i], a1, bq[i].z, bq[i].w);
+  }
+}
+
+// Row sums (B columns 0 + 1) of the four accumulator sets: (row g, row g+8).
+__device__ __forceinline__ float2 unit_rows(const float (&d)[4][4]) {
+  return make_float2(((d[0][0] + d[0][1]) + (d[1][0] + d[1][1])) + ((d[2][0] + d[2][1]) + (d[3][0] + d[3][1])),
+                     ((d[0][2] + d[0][3]) + (d[1][2] + d[1][3])) + ((d[2][2] + d[2][3]) + (d[3][2] + d[3][3])));
+}
+
+// Pack 8 fp32 values (already scaled by 2^e) into f16 hi and lo 16-byte units.
+__device__ __forceinline__ void pack_hi_lo(const float (&v)[8], uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half h0, l0, h1, l1;
+    split_f16(v[2 * i], h0, l0);
+    split_f16(v[2 * i + 1], h1, l1);
+    h[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+    l[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Work split shared by host and device (see the header comment).
+struct DecodeSplit {
+  int grid, K;
+  __host__ __device__ int n_gate() const { return K * kTilesPerExpert; }
+  __host__ __device__ int down_tiles_of(int c) const {  // down tiles c, c+grid, ... < 160
+    return kDownTiles / grid + (c < kDownTiles % grid ? 1 : 0);
+  }
+  __host__ __device__ int down_before(int c) const {  // down tiles owned by CTAs < c (closed form)
+    const int r = kDownTiles % grid;
+    return (kDownTiles / grid) * c + (c < r ? c : r);
+  }
+  __host__ __device__ int gate_start(int c) const {  // 4*x in units of quarter gate tiles
+    if (c >= grid) return n_gate();
+    const long long tot4 = 4LL * n_gate() + static_cast<long long>(kDownTiles) * K;
+    long long s4 = tot4 * c / grid - static_cast<long long>(down_before(c)) * K;
+    long long s = s4 / 4;
+    if (s < 0) s = 0;
+    if (s > n_gate()) s = n_gate();
+    return static_cast<int>(s);
+  }
+};
+
+struct PSmem {  // byte offsets of the dynamic shared-memory map of one CTA
+  int gate, down, hst, x_hi, x_lo, part, bar, eoff, red, cw, total;
+};
+
+__host__ __device__ inline PSmem psmem_map(int n_gate_tiles, int n_down_tiles, int K) {
+  PSmem m;
+  m.gate = 0;
+  m.down = n_gate_tiles * kTileBytes;
+  int end = m.down + n_down_tiles * K * (kDnWBytes + kDnSBytes);
+  // Phase 2 stages h (hi/lo) in the gate-tile region, which is free by then,
+  // or after the down rows when the gate-tile region is too small.
+  const int hneed = 2 * kHUnitsMax * 16 + 64;
+  m.hst = m.down >= hneed ? 0 : end;
+  if (end < m.hst + hneed) end = m.hst + hneed;
+  m.x_hi = (end + 127) / 128 * 128;
+  m.x_lo = m.x_hi + kXUnits * 16 + 64;
+  m.part = m.x_lo + kXUnits * 16;
+  const int part_bytes1 = kMaxGateTiles * 20 * 16 * 4;               // phase-1 unit partials
+  const int part_bytes2 = kMaxDownTiles * kFastMaxK * 5 * 16 * 4;    // phase-2 unit partials
+  m.bar = m.part + (part_bytes1 > part_bytes2 ? part_bytes1 : part_bytes2);
+  m.eoff = m.bar + (kMaxGateTiles + kMaxDownTiles) * 8;
+  m.red = m.eoff + kFastMaxK * 8;
+  m.cw = m.red + 64 * 4;
+  m.total = m.cw + 3 * kFastMaxK * 4;
+  return m;
+}
+
+template <bool kXF32>
+__global__ void __launch_bounds__(kPThreads, 1)
+    moe_decode_persistent(const uint8_t* __restrict__ table, int64_t n_blocks, const int32_t* __restrict__ sidx,
+                          const float* __restrict__ s2, const float* __restrict__ coef, const void* __restrict__ x,
+                          float* h, float* __restrict__ out, int K) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DecodeSplit sp{static_cast<int>(gridDim.x), K};
+  const int c = blockIdx.x;
+  const int g0 = sp.gate_start(c);
+  const int ng = sp.gate_start(c + 1) - g0;
+  const int nd = sp.down_tiles_of(c);
+  const PSmem M = psmem_map(ng, nd, K);
+  uint4* xh = reinterpret_cast<uint4*>(smem + M.x_hi);
+  uint4* xl = reinterpret_cast<uint4*>(smem + M.x_lo);
+  float* part = reinterpret_cast<float*>(smem + M.part);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + M.bar);  // [0, ng) gate tiles, [kMaxGateTiles, +nd) down
+  float* red = reinterpret_cast<float*>(smem + M.red);
+  float* cw = reinterpret_cast<float*>(smem + M.cw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  // Per-expert parameters, loaded once by K threads in parallel: block
+  // offset (-1 if out of range), ws2 gate/up, coef * ws2_down (NaN if invalid).
+  int64_t* eoff = reinterpret_cast<int64_t*>(smem + M.eoff);
+  float* ws_g = cw + kFastMaxK;
+  float* ws_u = cw + 2 * kFastMaxK;
+  if (threadIdx.x < K) {
+    const int j = threadIdx.x;
+    const int64_t b = sidx[j];
+    const bool ok = block_ok(b, n_blocks);
+    eoff[j] = ok ? b * kBlock : -1;
+    ws_g[j] = s2[3 * j + 0];
+    ws_u[j] = s2[3 * j + 1];
+    cw[j] = ok ? coef[j] * s2[3 * j + 2] : __int_as_float(0x7fc00000);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ng; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < nd; ++i) mbar_init(&bar[kMaxGateTiles + i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // Arm the barriers (lane i < ng: gate tile i; lane ng + i: down tile i).
+    if (lane < ng) {
+      mbar_arrive_expect_tx(&bar[lane], eoff[(g0 + lane) / kTilesPerExpert] >= 0 ? kTileBytes : 0);
+    } else if (lane < ng + nd) {
+      uint32_t tx = 0;
+      for (int j = 0; j < K; ++j) tx += eoff[j] >= 0 ? kDnWBytes + kDnSBytes : 0;
+      mbar_arrive_expect_tx(&bar[kMaxGateTiles + lane - ng], tx);
+    }
+    __syncwarp();
+    // Copies: 4 per gate tile, then 2 per (down tile, expert); lane q issues q, q+32, ...
+    const int n_copies = 4 * ng + 2 * K * nd;
+    for (int q = lane; q < n_copies; q += 32) {
+      if (q < 4 * ng) {
+        const int i = q >> 2, piece = q & 3;
+        const int T = g0 + i;
+        const int64_t off = eoff[T / kTilesPerExpert];
+        if (off < 0) continue;
+        const int64_t f0 = static_cast<int64_t>(T % kTilesPerExpert) * 8;
+        const uint8_t* blk = table + off;
+        uint8_t* dst = smem + M.gate + i * kTileBytes;
+        if (piece == 0) bulk_g2s(dst, blk + kOGW + f0 * 1280, 8 * 1280, &bar[i]);
+        else if (piece == 1) bulk_g2s(dst + 8 * 1280, blk + kOUW + f0 * 1280, 8 * 1280, &bar[i]);
+        else if (piece == 2) bulk_g2s(dst + 16 * 1280, blk + kOGS + f0 * 160, 8 * 160, &bar[i]);
+        else bulk_g2s(dst + 16 * 1280 + 1280, blk + kOUS + f0 * 160, 8 * 160, &bar[i]);
+      } else {
+        const int r = q - 4 * ng;
+        const int i = r / (2 * K), j = (r / 2) % K, piece = r & 1;
+        const int64_t off = eoff[j];
+        if (off < 0) continue;
+        const int64_t r0 = static_cast<int64_t>(c + i * sp.grid) * 16;
+        const uint8_t* blk = table + off;
+        uint8_t* dst = smem + M.down + (i * K + j) * (kDnWBytes + kDnSBytes);
+        if (piece == 0) bulk_g2s(dst, blk + kODW + r0 * (kInter / 2), kDnWBytes, &bar[kMaxGateTiles + i]);
+        else bulk_g2s(dst + kDnWBytes, blk + kODS + r0 * (kInter / 16), kDnSBytes, &bar[kMaxGateTiles + i]);
+      }
+    }
+  }
+
+  // ---- phase 1: x as f16 hi/lo in B-fragment order (unit u = (chunk, q, t))
+  int ex = 0;
+  {
+    float xv[8];
+    float mx = 0.f;
+    const int u = threadIdx.x;
+    if (u < kXUnits) {
+      const int xk0 = (u >> 4) * 128 + (u & 3) * 32 + ((u >> 2) & 3) * 8;
+      if (kXF32) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + xk0);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + xk0 + 4);
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+      } else {
+        const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + xk0);
+        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xv[2 * i] = bf16_bits_to_f32(rr[i] & 0xffffu);
+          xv[2 * i + 1] = bf16_bits_to_f32(rr[i] >> 16);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float a = fabsf(xv[i]);
+        mx = (isnan(a) || a > mx) ? a : mx;
+      }
+    }
+    ex = f16_prescale_exp(block_max(mx, red));
+    if (u < kXUnits) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = scale_pow2(xv[i], ex);
+      pack_hi_lo(xv, xh[u], xl[u]);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 1: (gate tile, 64-byte chunk) units, 20 chunks per tile
+  for (int u = warp; u < ng * 20; u += kPWarps) {
+    const int i = u / 20, ch = u % 20;
+    if (!mbar_wait(&bar[i], 0)) note_timeout();
+    const uint8_t* tile = smem + M.gate + i * kTileBytes;
+    const uint4 ra = lds128(tile + g * 1280 + 64 * ch + 16 * t);
+    const uint4 rb = lds128(tile + 8 * 1280 + g * 1280 + 64 * ch + 16 * t);
+    const uint32_t sa = lds16(tile + 16 * 1280 + g * 160 + 8 * ch + 2 * t);
+    const uint32_t sb = lds16(tile + 16 * 1280 + 1280 + g * 160 + 8 * ch + 2 * t);
+    uint4 bq[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+      const int uu = (ch * 4 + qq) * 4 + t;
+      bq[qq] = g == 0 ? xh[uu] : (g == 1 ? xl[uu] : make_uint4(0, 0, 0, 0));
+    }
+    float d[4][4] = {};
+    mma_chunk(d, ra, rb, sa, sb, bq);
+    if (t == 0) {
+      const float2 r = unit_rows(d);
+      part[u * 16 + g] = r.x;
+      part[u * 16 + 8 + g] = r.y;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < ng * 8) {
+    const int i = threadIdx.x >> 3, f = threadIdx.x & 7;
+    const int T = g0 + i;
+    const int j = T / kTilesPerExpert;
+    float gs = 0.f, us = 0.f;
+    for (int ch = 0; ch < 20; ++ch) {
+      gs += part[(i * 20 + ch) * 16 + f];
+      us += part[(i * 20 + ch) * 16 + 8 + f];
+    }
+    const float gg = scale_pow2(gs, -ex) * ws_g[j];
+    const float uu = scale_pow2(us, -ex) * ws_u[j];
+    const float hv = gg / (1.0f + expf(-gg)) * uu;
+    h[j * kInter + (T % kTilesPerExpert) * 8 + f] = eoff[j] >= 0 ? hv : __int_as_float(0x7fc00000);
+  }
+
+  cooperative_groups::this_grid().sync();  // every h row is written
+
+  // ---- phase 2: B = coef_j * ws2_d_j * h_j as f16 hi/lo units (unit u = j*80 + (c, q, t))
+  uint4* hh = reinterpret_cast<uint4*>(smem + M.hst);
+  uint4* hl = reinterpret_cast<uint4*>(smem + M.hst + kHUnitsMax * 16 + 64);
+  const int n_units = K * (kInter / 8);
+  constexpr int kMaxUnitsPerThread = (kHUnitsMax + kPThreads - 1) / kPThreads;  // 2
+  float hv[kMaxUnitsPerThread][8];
+  float mx = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxUnitsPerThread; ++k) {
+    const int u = threadIdx.x + k * kPThreads;
+    if (u < n_units) {
+      const int j = u / 80, rem = u % 80;
+      const int n0 = (rem >> 4) * 128 + (rem & 3) * 32 + ((rem >> 2) & 3) * 8;
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(h + j * kInter + n0));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(h + j * kInter + n0 + 4));
+      const float m = cw[j];
+      hv[k][0] = a.x * m; hv[k][1] = a.y * m; hv[k][2] = a.z * m; hv[k][3] = a.w * m;
+      hv[k][4] = b.x * m; hv[k][5] = b.y * m; hv[k][6] = b.z * m; hv[k][7] = b.w * m;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float aa = fabsf(hv[k][i]);
+        mx = (isnan(aa) || aa > mx) ? aa : mx;
+      }
+    }
+  }
+  const float hmax = block_max(mx, red);
+  const int eh = f16_prescale_exp(hmax);
+#pragma unroll
+  for (int k = 0; k < kMaxUnitsPerThread; ++k) {
+    const int u = threadIdx.x + k * kPThreads;
+    if (u < n_units) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hv[k][i] = scale_pow2(hv[k][i], eh);
+      pack_hi_lo(hv[k], hh[u], hl[u]);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 2: (down tile, expert, 64-byte chunk) units, 5K per down tile
+  const int per_tile = 5 * K;
+  for (int u = warp; u < nd * per_tile; u += kPWarps) {
+    const int i = u / per_tile, p = u % per_tile;
+    const int j = p / 5, ch = p % 5;
+    if (!mbar_wait(&bar[kMaxGateTiles + i], 0)) note_timeout();
+    const uint8_t* wj = smem + M.down + (i * K + j) * (kDnWBytes + kDnSBytes);
+    const uint4 ra = lds128(wj + g * (kInter / 2) + 64 * ch + 16 * t);
+    const uint4 rb = lds128(wj + (g + 8) * (kInter / 2) + 64 * ch + 16 * t);
+    const uint32_t sa = lds16(wj + kDnWBytes + g * (kInter / 16) + 8 * ch + 2 * t);
+    const uint32_t sb = lds16(wj + kDnWBytes + (g + 8) * (kInter / 16) + 8 * ch + 2 * t);
+    uint4 bq[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+      const int uu = (j * 5 + ch) * 16 + qq * 4 + t;
+      bq[qq] = g == 0 ? hh[uu] : (g == 1 ? hl[uu] : make_uint4(0, 0, 0, 0));
+    }
+    float d[4][4] = {};
+    mma_chunk(d, ra, rb, sa, sb, bq);
+    if (t == 0) {
+      const float2 r = unit_rows(d);
+      part[u * 16 + g] = r.x;
+      part[u * 16 + 8 + g] = r.y;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nd * 16) {
+    const int i = threadIdx.x >> 4, row = threadIdx.x & 15;
+    float acc = 0.f;
+    for (int p = 0; p < per_tile; ++p) acc += part[(i * per_tile + p) * 16 + row];
+    out[(c + i * sp.grid) * 16 + row] = isnan(hmax) ? hmax : scale_pow2(acc, -eh);
+  }
+}
+
+static int launch_moe_decode_fast(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                                  const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
+                                  cudaStream_t st, const DeviceInfo* dev, int grid) {
+  // shared memory: the largest per-CTA map of this split
+  const DecodeSplit sp{grid, K};
+  int smem = 0;
+  for (int c = 0; c < grid; ++c) {
+    const PSmem m = psmem_map(sp.gate_start(c + 1) - sp.gate_start(c), sp.down_tiles_of(c), K);
+    if (m.total > smem) smem = m.total;
+  }
+  auto fn = x_dtype == QFN_DTYPE_F32 ? moe_decode_persistent<true> : moe_decode_persistent<false>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "decode smem attribute (%d B): %s", smem, cudaGetErrorString(e));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, fn, table, n_blocks, sidx, s2, coef, x, h_buf, out, K);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_decode_persistent launch: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode_persistent");
+}
+
+// Whether the persistent path fits this device: per-CTA tile counts within the
+// static bounds and the shared-memory map within the opt-in limit.
+static bool persistent_fits(int K, const DeviceInfo* dev) {
+  if (K > kFastMaxK) return false;
+  const int grid = dev->sm_count;
+  const DecodeSplit sp{grid, K};
+  for (int c = 0; c < grid; ++c) {
+    const int ng = sp.gate_start(c + 1) - sp.gate_start(c), nd = sp.down_tiles_of(c);
+    if (ng > kMaxGateTiles || nd > kMaxDownTiles || ng + nd > 32) return false;
+    if (static_cast<size_t>(psmem_map(ng, nd, K).total) > dev->smem_optin) return false;
+  }
+  return true;
+}
+
+static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                             const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
+                             cudaStream_t st, int variant) {
+  DeviceInfo* dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  // The persistent path keeps a CTA's whole share of the layer in shared memory.
+  const bool fits = persistent_fits(K, dev);
+  if (variant == 1 && !fits)
+    return set_error(QFN_ERR_UNSUPPORTED, "tensor-core decode path needs K <= %d (and a 148-SM-class device)",
+                     kFastMaxK);
+  if (variant == 1 || (variant == 0 && fits))
+    return launch_moe_decode_fast(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st, dev,
+                                  dev->sm_count);
+  return launch_moe_decode_generic(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st);
 }
 
 }  // namespace qfn
 
 using namespace qfn;
 
-extern "C" int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
-                              const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
-                              qfn_stream_t stream) {
+static int check_decode_args(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                             const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K) {
   QFN_REQUIRE(table && sidx && s2 && coef && x && h_buf && out, QFN_ERR_INVALID_ARG,
               "qfn_moe_decode: null pointer");
   QFN_REQUIRE(n_blocks > 0, QFN_ERR_INVALID_ARG, "qfn_moe_decode: n_blocks=%lld", (long long)n_blocks);
@@ -239,7 +700,37 @@ extern "C" int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int3
               QFN_MAX_TOPK);
   QFN_REQUIRE(x_dtype == QFN_DTYPE_F32 || x_dtype == QFN_DTYPE_BF16, QFN_ERR_INVALID_ARG,
               "qfn_moe_decode: bad x_dtype %d", x_dtype);
-  QFN_REQUIRE(aligned(table, 16) && aligned(h_buf, 16) && aligned(x, x_dtype == QFN_DTYPE_F32 ? 16 : 8),
-              QFN_ERR_ALIGNMENT, "qfn_moe_decode: table/h_buf must be 16-byte aligned, x 16 (f32) or 8 (bf16)");
-  return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, as_stream(stream));
+  QFN_REQUIRE(aligned(table, 16) && aligned(h_buf, 16) && aligned(x, 16), QFN_ERR_ALIGNMENT,
+              "qfn_moe_decode: table, h_buf and x must be 16-byte aligned");
+  return QFN_OK;
+}
+
+extern "C" int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                              const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
+                              qfn_stream_t stream) {
+  int rc = check_decode_args(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K);
+  if (rc) return rc;
+  return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, as_stream(stream), 0);
+}
+
+extern "C" int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                                      const float* coef, const void* x, int x_dtype, float* h_buf, float* out,
+                                      int K, int variant, qfn_stream_t stream) {
+  int rc = check_decode_args(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K);
+  if (rc) return rc;
+  QFN_REQUIRE(variant >= 0 && variant <= 2, QFN_ERR_INVALID_ARG, "qfn_moe_decode_variant: variant %d", variant);
+  QFN_REQUIRE(variant != 1 || K <= kFastMaxK, QFN_ERR_UNSUPPORTED,
+              "qfn_moe_decode_variant: the tensor-core path takes K <= %d", kFastMaxK);
+  return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, as_stream(stream), variant);
+}
+
+extern "C" int qfn_device_status(unsigned int* status, int clear) {
+  QFN_REQUIRE(status, QFN_ERR_INVALID_ARG, "qfn_device_status: null pointer");
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_decode_status, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_decode_status, &zero, sizeof(unsigned int));
+  }
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_device_status: %s", cudaGetErrorString(e));
+  return QFN_OK;
 }

@@ -42,6 +42,14 @@ def moe_decode(slots_u8, sidx, s2, coef, x, h_buf, out_buf):
     -> new fp32 [2560] = sum_j coef_j * down_j(silu(gate_j x) * up_j x).
     Queued on torch's current stream; graph-capturable.
     """
+    return _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, 0)
+
+
+VARIANT_AUTO, VARIANT_TENSOR_CORE, VARIANT_CUDA_CORE = 0, 1, 2
+
+
+def _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant):
+    """moe_decode with an explicit kernel path (tests / measurements)."""
     require_cuda("slots_u8", slots_u8, torch.uint8)
     require_cuda("sidx", sidx, torch.int32)
     require_cuda("s2", s2, torch.float32)
@@ -65,10 +73,10 @@ def moe_decode(slots_u8, sidx, s2, coef, x, h_buf, out_buf):
             raise ValueError(f"{name} is on {t.device}, slots_u8 on {dev}")
     out = torch.empty(HID, dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
-        rc = lib().qfn_moe_decode(slots_u8.data_ptr(), slots_u8.shape[0], sidx.data_ptr(), s2.data_ptr(),
-                                  coef.data_ptr(), x.data_ptr(),
-                                  DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16,
-                                  h_buf.data_ptr(), out.data_ptr(), K, stream_of(out))
+        rc = lib().qfn_moe_decode_variant(slots_u8.data_ptr(), slots_u8.shape[0], sidx.data_ptr(),
+                                          s2.data_ptr(), coef.data_ptr(), x.data_ptr(),
+                                          DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16,
+                                          h_buf.data_ptr(), out.data_ptr(), K, variant, stream_of(out))
     check(rc, "qfn_moe_decode")
     return out
 
