@@ -121,6 +121,25 @@ int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t
                            qfn_stream_t stream);
 
 /*
+ * qfn_moe_decode_noalloc -- qfn_moe_decode for callers that cannot allocate
+ * device memory when they run a step (memory planned once up front, a
+ * foreign-language binding without a device allocator, a loop that forbids
+ * allocator calls).  No counterpart in the reference.  It takes no h_buf:
+ * the h scratch is a file-scope device array of QFN_MAX_TOPK x 640 floats
+ * (80 KB) that every device loading the library holds until exit.  The
+ * entry point calls no allocator.  Its first call on a device resolves the
+ * array's device address (cudaGetSymbolAddress): make that first call before
+ * any stream capture.  All calls on a device share the array, so calls that
+ * overlap on the GPU (different streams, no ordering between them) race;
+ * calls in one stream are safe.  h is fully rewritten by every call, so
+ * nothing needs clearing.  1 <= K <= QFN_MAX_TOPK, otherwise
+ * QFN_ERR_UNSUPPORTED.  Other arguments as for qfn_moe_decode.
+ */
+int qfn_moe_decode_noalloc(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
+                           const float* s2, const float* coef, const void* x, int x_dtype,
+                           float* out, int K, qfn_stream_t stream);
+
+/*
  * qfn_device_status -- read (and with clear != 0, reset) the decode kernels'
  * device status word of the current device: bit 0 = a bounded wait on a
  * shared-memory barrier ran out (the outputs of that call are invalid).

@@ -25,6 +25,7 @@ SIGNATURES = {
     "qfn_block_deq": [_P, _P, _P, _P, _P, _P],
     "qfn_moe_decode": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _P],
     "qfn_moe_decode_variant": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _I, _P],
+    "qfn_moe_decode_noalloc": [_P, _I64, _P, _P, _P, _P, _I, _P, _I, _P],
     "qfn_device_status": [_P, _I],
     "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
 }

@@ -16,6 +16,8 @@
 //    were complete before gate_up started), then wait for gate_up's h.
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "host.cuh"
 
@@ -733,4 +735,48 @@ extern "C" int qfn_device_status(unsigned int* status, int clear) {
   }
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_device_status: %s", cudaGetErrorString(e));
   return QFN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.  Some callers cannot allocate device memory at
+// the point where they run a decode step: a runtime whose device memory is
+// planned once up front (an 8 GB card running a 63 GiB model has no slack),
+// an embedding through a foreign-language FFI that has no binding to a device
+// allocator, or a real-time loop that forbids allocator calls.  For them the
+// h scratch lives in this file-scope device array instead of a caller buffer.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kNoAllocMaxK = QFN_MAX_TOPK;  // 32 experts x 640 floats = 80 KB per device
+__device__ __align__(256) float g_noalloc_h[kNoAllocMaxK * qfn::kInter];
+float* g_noalloc_ptr[64] = {};
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int qfn_moe_decode_noalloc(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                                      const float* coef, const void* x, int x_dtype, float* out, int K,
+                                      qfn_stream_t stream) {
+  QFN_REQUIRE(K >= 1 && K <= kNoAllocMaxK, QFN_ERR_UNSUPPORTED,
+              "qfn_moe_decode_noalloc: K=%d outside [1, %d] (the static scratch holds %d experts)", K, kNoAllocMaxK,
+              kNoAllocMaxK);
+  QFN_REQUIRE(table && sidx && s2 && coef && x && out, QFN_ERR_INVALID_ARG, "qfn_moe_decode_noalloc: null pointer");
+  DeviceInfo* dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  float* h = nullptr;
+  {
+    // First call on a device: resolve the device address of the scratch array
+    // (host code must not use the symbol itself: that is a host-side stand-in).
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev->device]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_h);
+      if (e != cudaSuccess)
+        return set_error(QFN_ERR_CUDA, "qfn_moe_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_noalloc_ptr[dev->device] = static_cast<float*>(p);
+    }
+    h = g_noalloc_ptr[dev->device];
+  }
+  rc = check_decode_args(table, n_blocks, sidx, s2, coef, x, x_dtype, h, out, K);
+  if (rc) return rc;
+  return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h, out, K, as_stream(stream), 0);
 }
