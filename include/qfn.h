@@ -102,9 +102,10 @@ int qfn_block_deq(const uint8_t* blk, const float s2[3], float* gate, float* up,
  *           it holds h, as in the reference.
  *   out:    f32[2560] device; written (not accumulated).
  *   1 <= K <= QFN_MAX_TOPK.
- *   K <= 10 runs the tensor-core path (two programmatically dependent
- *   launches); larger K runs the CUDA-core path.  Results are bit-identical
- *   between calls with the same inputs (fixed reduction order).
+ *   Runs the CUDA-core path (two launches, the second a programmatic
+ *   dependent of the first); qfn_moe_decode_variant selects the tensor-core
+ *   path.  Results are bit-identical between calls with the same inputs
+ *   (fixed reduction order).
  */
 int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                    const float* s2, const float* coef, const void* x, int x_dtype,
@@ -113,7 +114,10 @@ int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
 /*
  * qfn_moe_decode_variant -- qfn_moe_decode with the kernel path chosen by the
  * caller (no counterpart in the reference; for tests and measurements):
- * variant 0 = automatic, 1 = tensor-core path (K <= 10), 2 = CUDA-core path.
+ * variant 0 = automatic (currently the CUDA-core path), 1 = tensor-core path
+ * (one cooperative persistent launch: tcgen05 block-scaled FP4 MMA for
+ * gate/up, mma.sync for down; K <= 10; weight block scales must be positive),
+ * 2 = CUDA-core path.
  */
 int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                            const float* s2, const float* coef, const void* x, int x_dtype,

@@ -272,6 +272,7 @@ constexpr int kHUnitsMax = kFastMaxK * (kInter / 128) * 16;  // 800
 __device__ unsigned int g_decode_status = 0;
 
 __device__ __forceinline__ void note_timeout() { atomicOr(&g_decode_status, kStatusTimeout); }
+constexpr unsigned kStatusNegativeScale = 2u;
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
@@ -373,64 +374,94 @@ struct DecodeSplit {
   }
 };
 
-struct PSmem {  // byte offsets of the dynamic shared-memory map of one CTA
-  int gate, down, hst, x_hi, x_lo, part, bar, eoff, red, cw, total;
+struct PSmem {  // byte offsets (from the 1024-aligned base) of the dynamic shared-memory map of one CTA
+  int a, b, gsc, tsc, gu, down, hst, part, bar, eoff, red, cw, slot, total;
 };
+
+constexpr int kTerms = 8;              // e2m1 terms of an activation vector (B rows)
+constexpr int kARowGroupBytes = 10240; // 8 rows x 10 K-chunks x 128 B (SWIZZLE_128B atoms)
+constexpr int kAReach = 16 * kARowGroupBytes;  // bytes an M=128 MMA operand spans from its base
+constexpr int kKSteps = kHid / 64;     // 40 MMA K-steps (K = 64 e2m1 each)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmD = 0, kTmSfa = 32, kTmSfb = 32 + 4 * kKSteps;
 
 __host__ __device__ inline PSmem psmem_map(int n_gate_tiles, int n_down_tiles, int K) {
   PSmem m;
-  m.gate = 0;
-  m.down = n_gate_tiles * kTileBytes;
+  m.a = 0;                                         // A: 2 row groups (gate, up) per gate tile
+  m.b = 2 * n_gate_tiles * kARowGroupBytes;        // B: x terms, one 8-row group (1024-aligned)
+  m.gsc = m.b + kARowGroupBytes;                   // gate-tile scales, natural [tile][gate|up][8][160]
+  m.tsc = m.gsc + n_gate_tiles * 2 * 8 * (kHid / 16);  // term scales, natural [8][160]
+  m.gu = m.tsc + kTerms * (kHid / 16);             // 128 gate/up row values
+  m.down = m.gu + 128 * 4;
   int end = m.down + n_down_tiles * K * (kDnWBytes + kDnSBytes);
   // Phase 2 stages h (hi/lo) in the gate-tile region, which is free by then,
-  // or after the down rows when the gate-tile region is too small.
+  // or after the down rows when that region is too small.
   const int hneed = 2 * kHUnitsMax * 16 + 64;
   m.hst = m.down >= hneed ? 0 : end;
   if (end < m.hst + hneed) end = m.hst + hneed;
-  m.x_hi = (end + 127) / 128 * 128;
-  m.x_lo = m.x_hi + kXUnits * 16 + 64;
-  m.part = m.x_lo + kXUnits * 16;
-  const int part_bytes1 = kMaxGateTiles * 20 * 16 * 4;               // phase-1 unit partials
-  const int part_bytes2 = kMaxDownTiles * kFastMaxK * 5 * 16 * 4;    // phase-2 unit partials
-  m.bar = m.part + (part_bytes1 > part_bytes2 ? part_bytes1 : part_bytes2);
-  m.eoff = m.bar + (kMaxGateTiles + kMaxDownTiles) * 8;
+  m.part = (end + 15) / 16 * 16;
+  m.bar = m.part + kMaxDownTiles * kFastMaxK * 5 * 16 * 4;
+  m.eoff = m.bar + (kMaxGateTiles + kMaxDownTiles + 1) * 8;
   m.red = m.eoff + kFastMaxK * 8;
   m.cw = m.red + 64 * 4;
-  m.total = m.cw + 3 * kFastMaxK * 4;
+  m.slot = m.cw + 4 * kFastMaxK * 4;  // cw, ws_g, ws_u (floats) and block indices (ints)
+  end = m.slot + 16;
+  // the M = 128 A operand reads 16 row groups from its base (rows past 2 * n_gate_tiles * 8 are
+  // never used, but must lie inside the allocation)
+  m.total = (end > kAReach ? end : kAReach) + 1024;  // + alignment slack for the 1024-byte base
   return m;
 }
 
 template <bool kXF32>
 __global__ void __launch_bounds__(kPThreads, 1)
-    moe_decode_persistent(const uint8_t* __restrict__ table, int64_t n_blocks, const int32_t* __restrict__ sidx,
-                          const float* __restrict__ s2, const float* __restrict__ coef, const void* __restrict__ x,
-                          float* h, float* __restrict__ out, int K) {
-  extern __shared__ __align__(128) uint8_t smem[];
+    moe_decode_persistent(const __grid_constant__ CUtensorMap gate_map, const uint8_t* __restrict__ table,
+                          int64_t n_blocks, const int32_t* __restrict__ sidx, const float* __restrict__ s2,
+                          const float* __restrict__ coef, const void* __restrict__ x, float* h,
+                          float* __restrict__ out, int K) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const DecodeSplit sp{static_cast<int>(gridDim.x), K};
   const int c = blockIdx.x;
   const int g0 = sp.gate_start(c);
   const int ng = sp.gate_start(c + 1) - g0;
   const int nd = sp.down_tiles_of(c);
   const PSmem M = psmem_map(ng, nd, K);
-  uint4* xh = reinterpret_cast<uint4*>(smem + M.x_hi);
-  uint4* xl = reinterpret_cast<uint4*>(smem + M.x_lo);
   float* part = reinterpret_cast<float*>(smem + M.part);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + M.bar);  // [0, ng) gate tiles, [kMaxGateTiles, +nd) down
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + M.bar);  // [0,ng) gate, [6,6+nd) down, [8] MMA done
+  uint64_t* mma_bar = bar + kMaxGateTiles + kMaxDownTiles;
   float* red = reinterpret_cast<float*>(smem + M.red);
   float* cw = reinterpret_cast<float*>(smem + M.cw);
+  float* gu = reinterpret_cast<float*>(smem + M.gu);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + M.slot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+
+  // x loads first (they depend on nothing), so their latency overlaps the
+  // parameter loads below.  Thread u owns k in [4u, 4u + 4).
+  const int u = threadIdx.x;
+  float xv[4];
+  if (kXF32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + 4 * u);
+    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+  } else {
+    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + 4 * u);
+    xv[0] = bf16_bits_to_f32(r.x & 0xffffu); xv[1] = bf16_bits_to_f32(r.x >> 16);
+    xv[2] = bf16_bits_to_f32(r.y & 0xffffu); xv[3] = bf16_bits_to_f32(r.y >> 16);
+  }
+  if (threadIdx.x == 32) prefetch_tensormap(&gate_map);
 
   // Per-expert parameters, loaded once by K threads in parallel: block
   // offset (-1 if out of range), ws2 gate/up, coef * ws2_down (NaN if invalid).
   int64_t* eoff = reinterpret_cast<int64_t*>(smem + M.eoff);
   float* ws_g = cw + kFastMaxK;
   float* ws_u = cw + 2 * kFastMaxK;
+  int* eblk = reinterpret_cast<int*>(cw + 3 * kFastMaxK);
   if (threadIdx.x < K) {
     const int j = threadIdx.x;
     const int64_t b = sidx[j];
     const bool ok = block_ok(b, n_blocks);
     eoff[j] = ok ? b * kBlock : -1;
+    eblk[j] = ok ? static_cast<int>(b) : 0;
     ws_g[j] = s2[3 * j + 0];
     ws_u[j] = s2[3 * j + 1];
     cw[j] = ok ? coef[j] * s2[3 * j + 2] : __int_as_float(0x7fc00000);
@@ -438,6 +469,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < ng; ++i) mbar_init(&bar[i], 1);
     for (int i = 0; i < nd; ++i) mbar_init(&bar[kMaxGateTiles + i], 1);
+    mbar_init(mma_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -452,21 +484,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mbar_arrive_expect_tx(&bar[kMaxGateTiles + lane - ng], tx);
     }
     __syncwarp();
-    // Copies: 4 per gate tile, then 2 per (down tile, expert); lane q issues q, q+32, ...
+    // Copies: 4 per gate tile (gate rows, up rows: 3-D tensor boxes into the
+    // SWIZZLE_128B operand layout; gate and up scales: bulk), then 2 per
+    // (down tile, expert); lane q issues copies q, q+32, ...
     const int n_copies = 4 * ng + 2 * K * nd;
     for (int q = lane; q < n_copies; q += 32) {
       if (q < 4 * ng) {
         const int i = q >> 2, piece = q & 3;
         const int T = g0 + i;
-        const int64_t off = eoff[T / kTilesPerExpert];
+        const int j = T / kTilesPerExpert;
+        const int64_t off = eoff[j];
         if (off < 0) continue;
-        const int64_t f0 = static_cast<int64_t>(T % kTilesPerExpert) * 8;
-        const uint8_t* blk = table + off;
-        uint8_t* dst = smem + M.gate + i * kTileBytes;
-        if (piece == 0) bulk_g2s(dst, blk + kOGW + f0 * 1280, 8 * 1280, &bar[i]);
-        else if (piece == 1) bulk_g2s(dst + 8 * 1280, blk + kOUW + f0 * 1280, 8 * 1280, &bar[i]);
-        else if (piece == 2) bulk_g2s(dst + 16 * 1280, blk + kOGS + f0 * 160, 8 * 160, &bar[i]);
-        else bulk_g2s(dst + 16 * 1280 + 1280, blk + kOUS + f0 * 160, 8 * 160, &bar[i]);
+        const int f0 = (T % kTilesPerExpert) * 8;
+        const int row0 = eblk[j] * 2160 + f0;  // table row of gate row f0 (2160 rows of 1280 B per block)
+        if (piece == 0) tma_load_3d(smem + M.a + (2 * i) * kARowGroupBytes, &gate_map, 0, row0, 0, &bar[i]);
+        else if (piece == 1) tma_load_3d(smem + M.a + (2 * i + 1) * kARowGroupBytes, &gate_map, 0, row0 + kInter, 0, &bar[i]);
+        else if (piece == 2) bulk_g2s(smem + M.gsc + i * 2560, table + off + kOGS + f0 * 160, 1280, &bar[i]);
+        else bulk_g2s(smem + M.gsc + i * 2560 + 1280, table + off + kOUS + f0 * 160, 1280, &bar[i]);
       } else {
         const int r = q - 4 * ng;
         const int i = r / (2 * K), j = (r / 2) % K, piece = r & 1;
@@ -479,65 +513,121 @@ __global__ void __launch_bounds__(kPThreads, 1)
         else bulk_g2s(dst + kDnWBytes, blk + kODS + r0 * (kInter / 16), kDnSBytes, &bar[kMaxGateTiles + i]);
       }
     }
+  } else if (warp == 1) {
+    tmem_alloc(tslot, kTmemCols);
   }
 
-  // ---- phase 1: x as f16 hi/lo in B-fragment order (unit u = (chunk, q, t))
-  int ex = 0;
+  // ---- phase 1: x -> kTerms e2m1 terms with ue4m3 scales per 16 k (the B
+  // operand).  Term t carries the column factor 2^(ex - 2t); block scales are
+  // rounded up so |residual / scale| <= 6.  Four threads share a 16-block.
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a = fabsf(xv[i]);
+    mx = (isnan(a) || a > mx) ? a : mx;
+  }
+  const float xmax = block_max(mx, red);
+  int ex = 0;  // 2^ex >= xmax / (6 * 448): term 0's block scales stay <= 448
+  if (xmax > 0.f && isfinite(xmax)) frexpf(xmax * (1.0f / 2688.0f), &ex);
   {
-    float xv[8];
-    float mx = 0.f;
-    const int u = threadIdx.x;
-    if (u < kXUnits) {
-      const int xk0 = (u >> 4) * 128 + (u & 3) * 32 + ((u >> 2) & 3) * 8;
-      if (kXF32) {
-        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + xk0);
-        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + xk0 + 4);
-        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
-      } else {
-        const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + xk0);
-        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          xv[2 * i] = bf16_bits_to_f32(rr[i] & 0xffffu);
-          xv[2 * i + 1] = bf16_bits_to_f32(rr[i] >> 16);
-        }
+    uint8_t* bt = smem + M.b;
+    uint8_t* tsc = smem + M.tsc;
+    const int cch = u >> 6, jj = (u & 63) >> 3, wb = 2 * (u & 7);  // K-chunk, 16-B chunk, byte in it
+#pragma unroll 1
+    for (int tt = 0; tt < kTerms; ++tt) {
+      const float F = scale_pow2(1.0f, ex - 2 * tt);
+      float a = fmaxf(fmaxf(fabsf(xv[0]), fabsf(xv[1])), fmaxf(fabsf(xv[2]), fabsf(xv[3])));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      uint32_t sb = 0;
+      float sF = 0.f;
+      if (a > 0.f) {
+        const float y = fmaxf(a / (6.0f * F), 1.0f / 512.0f);
+        sb = f32_to_e4m3_rn(y);
+        if (e4m3_to_f32(sb) < y && sb < 0x7eu) sb += 1;
+        sF = e4m3_to_f32(sb) * F;
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float a = fabsf(xv[i]);
-        mx = (isnan(a) || a > mx) ? a : mx;
-      }
-    }
-    ex = f16_prescale_exp(block_max(mx, red));
-    if (u < kXUnits) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xv[i] = scale_pow2(xv[i], ex);
-      pack_hi_lo(xv, xh[u], xl[u]);
+      const float inv = sF > 0.f ? 1.0f / sF : 0.f;
+      const uint32_t b0 = f32x2_to_e2m1(xv[0] * inv, xv[1] * inv);
+      const uint32_t b1 = f32x2_to_e2m1(xv[2] * inv, xv[3] * inv);
+      uint32_t hq[4];
+      e2m1x8_to_f16x2(b0 | (b1 << 8), hq);
+      const float2 q0 = f16x2_to_f32x2(hq[0]), q1 = f16x2_to_f32x2(hq[1]);
+      xv[0] = fmaf(-q0.x, sF, xv[0]);
+      xv[1] = fmaf(-q0.y, sF, xv[1]);
+      xv[2] = fmaf(-q1.x, sF, xv[2]);
+      xv[3] = fmaf(-q1.y, sF, xv[3]);
+      *reinterpret_cast<uint16_t*>(bt + cch * 1024 + tt * 128 + ((jj ^ tt) << 4) + wb) =
+          static_cast<uint16_t>(b0 | (b1 << 8));
+      if ((u & 3) == 0) tsc[tt * (kHid / 16) + (u >> 2)] = static_cast<uint8_t>(sb);
     }
   }
-  __syncthreads();
 
-  // ---- phase 1: (gate tile, 64-byte chunk) units, 20 chunks per tile
-  for (int u = warp; u < ng * 20; u += kPWarps) {
-    const int i = u / 20, ch = u % 20;
+  // ---- phase 1: wait for the gate tiles, scale factors -> TMEM, 40 MMAs
+  for (int i = 0; i < ng; ++i)
     if (!mbar_wait(&bar[i], 0)) note_timeout();
-    const uint8_t* tile = smem + M.gate + i * kTileBytes;
-    const uint4 ra = lds128(tile + g * 1280 + 64 * ch + 16 * t);
-    const uint4 rb = lds128(tile + 8 * 1280 + g * 1280 + 64 * ch + 16 * t);
-    const uint32_t sa = lds16(tile + 16 * 1280 + g * 160 + 8 * ch + 2 * t);
-    const uint32_t sb = lds16(tile + 16 * 1280 + 1280 + g * 160 + 8 * ch + 2 * t);
-    uint4 bq[4];
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  uint32_t neg = 0;
+  if (warp < 16) {
+    // TMEM lane l (of every 32-lane quadrant), column base + 4s + m1 holds the
+    // 4 scales of K-step s of operand row l + 32*m1.  Warp w writes quadrant
+    // w % 4, K-steps [10 (w / 4), +10).
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const int ks0 = 10 * (warp >> 2);
+    const uint8_t* gsc = smem + M.gsc;
+    const uint8_t* tsc = smem + M.tsc;
+    uint32_t va[40], vb[40];
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-      const int uu = (ch * 4 + qq) * 4 + t;
-      bq[qq] = g == 0 ? xh[uu] : (g == 1 ? xl[uu] : make_uint4(0, 0, 0, 0));
+    for (int m1 = 0; m1 < 4; ++m1) {
+      const int m = lane + 32 * m1;  // A row: row group m/8 = (tile, gate|up), row m%8
+      const int rg = m >> 3;
+      const bool live = rg < 2 * ng && eoff[(g0 + (rg >> 1)) / kTilesPerExpert] >= 0;
+      const uint8_t* ra = gsc + (rg >> 1) * 2560 + (rg & 1) * 1280 + (m & 7) * 160 + 4 * ks0;
+      const uint8_t* rb = tsc + m * 160 + 4 * ks0;
+#pragma unroll
+      for (int k = 0; k < 10; ++k) {
+        va[4 * k + m1] = live ? *reinterpret_cast<const uint32_t*>(ra + 4 * k) : 0x38383838u;  // 1.0 if not loaded
+        vb[4 * k + m1] = m < kTerms ? *reinterpret_cast<const uint32_t*>(rb + 4 * k) : 0u;
+        neg |= va[4 * k + m1];
+      }
     }
-    float d[4][4] = {};
-    mma_chunk(d, ra, rb, sa, sb, bq);
-    if (t == 0) {
-      const float2 r = unit_rows(d);
-      part[u * 16 + g] = r.x;
-      part[u * 16 + 8 + g] = r.y;
+    const uint32_t ca = tbase + lane_off + kTmSfa + 4 * ks0, cb = tbase + lane_off + kTmSfb + 4 * ks0;
+    tmem_st_x32(ca, *reinterpret_cast<const uint32_t(*)[32]>(&va[0]));
+    tmem_st_x8(ca + 32, *reinterpret_cast<const uint32_t(*)[8]>(&va[32]));
+    tmem_st_x32(cb, *reinterpret_cast<const uint32_t(*)[32]>(&vb[0]));
+    tmem_st_x8(cb + 32, *reinterpret_cast<const uint32_t(*)[8]>(&vb[32]));
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0 && ng > 0) {
+    const uint32_t idesc = idesc_mxf4nvf4(128, 16);
+    const uint32_t a0 = smem_u32(smem + M.a), b0 = smem_u32(smem + M.b);
+#pragma unroll 1
+    for (int ks = 0; ks < kKSteps; ++ks) {
+      const uint32_t koff = (ks >> 2) * 1024 + 32 * (ks & 3);
+      mma_mxf4nvf4(tbase + kTmD, umma_desc_sw128(a0 + koff, kARowGroupBytes), umma_desc_sw128(b0 + koff, 0), idesc,
+                   ks > 0, tbase + kTmSfa + 4 * ks, tbase + kTmSfb + 4 * ks);
+    }
+    mma_commit(mma_bar);
+  }
+  // A scale with its sign bit set is outside the ue4m3 range the tensor core reads.
+  const bool bad_scale = __syncthreads_or((neg & 0x80808080u) != 0);
+  if (ng > 0) {
+    if (!mbar_wait(mma_bar, 0)) note_timeout();
+    tc_fence_after();
+    if (warp < 4) {
+      uint32_t d[8];
+      tmem_ld_x8(tbase + (static_cast<uint32_t>(32 * warp) << 16) + kTmD, d);
+      float v = 0.f;
+#pragma unroll
+      for (int tt = 0; tt < kTerms; ++tt) v = fmaf(__uint_as_float(d[tt]), scale_pow2(1.0f, ex - 2 * tt), v);
+      gu[32 * warp + lane] = v;
     }
   }
   __syncthreads();
@@ -545,16 +635,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int i = threadIdx.x >> 3, f = threadIdx.x & 7;
     const int T = g0 + i;
     const int j = T / kTilesPerExpert;
-    float gs = 0.f, us = 0.f;
-    for (int ch = 0; ch < 20; ++ch) {
-      gs += part[(i * 20 + ch) * 16 + f];
-      us += part[(i * 20 + ch) * 16 + 8 + f];
-    }
-    const float gg = scale_pow2(gs, -ex) * ws_g[j];
-    const float uu = scale_pow2(us, -ex) * ws_u[j];
+    const float gg = gu[16 * i + f] * ws_g[j];
+    const float uu = gu[16 * i + 8 + f] * ws_u[j];
     const float hv = gg / (1.0f + expf(-gg)) * uu;
-    h[j * kInter + (T % kTilesPerExpert) * 8 + f] = eoff[j] >= 0 ? hv : __int_as_float(0x7fc00000);
+    const bool ok = eoff[j] >= 0 && isfinite(xmax) && !bad_scale;
+    h[j * kInter + (T % kTilesPerExpert) * 8 + f] = ok ? hv : __int_as_float(0x7fc00000);
   }
+  if (bad_scale && threadIdx.x == 0) atomicOr(&g_decode_status, kStatusNegativeScale);
 
   cooperative_groups::this_grid().sync();  // every h row is written
 
@@ -564,12 +651,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int n_units = K * (kInter / 8);
   constexpr int kMaxUnitsPerThread = (kHUnitsMax + kPThreads - 1) / kPThreads;  // 2
   float hv[kMaxUnitsPerThread][8];
-  float mx = 0.f;
+  mx = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxUnitsPerThread; ++k) {
-    const int u = threadIdx.x + k * kPThreads;
-    if (u < n_units) {
-      const int j = u / 80, rem = u % 80;
+    const int uu = threadIdx.x + k * kPThreads;
+    if (uu < n_units) {
+      const int j = uu / 80, rem = uu % 80;
       const int n0 = (rem >> 4) * 128 + (rem & 3) * 32 + ((rem >> 2) & 3) * 8;
       const float4 a = __ldcg(reinterpret_cast<const float4*>(h + j * kInter + n0));
       const float4 b = __ldcg(reinterpret_cast<const float4*>(h + j * kInter + n0 + 4));
@@ -587,19 +674,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int eh = f16_prescale_exp(hmax);
 #pragma unroll
   for (int k = 0; k < kMaxUnitsPerThread; ++k) {
-    const int u = threadIdx.x + k * kPThreads;
-    if (u < n_units) {
+    const int uu = threadIdx.x + k * kPThreads;
+    if (uu < n_units) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) hv[k][i] = scale_pow2(hv[k][i], eh);
-      pack_hi_lo(hv[k], hh[u], hl[u]);
+      pack_hi_lo(hv[k], hh[uu], hl[uu]);
     }
   }
   __syncthreads();
 
-  // ---- phase 2: (down tile, expert, 64-byte chunk) units, 5K per down tile
+  // ---- phase 2: (down tile, expert, 64-byte chunk) units, 5K per down tile (mma.sync)
   const int per_tile = 5 * K;
-  for (int u = warp; u < nd * per_tile; u += kPWarps) {
-    const int i = u / per_tile, p = u % per_tile;
+  for (int uu = warp; uu < nd * per_tile; uu += kPWarps) {
+    const int i = uu / per_tile, p = uu % per_tile;
     const int j = p / 5, ch = p % 5;
     if (!mbar_wait(&bar[kMaxGateTiles + i], 0)) note_timeout();
     const uint8_t* wj = smem + M.down + (i * K + j) * (kDnWBytes + kDnSBytes);
@@ -610,15 +697,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
     uint4 bq[4];
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) {
-      const int uu = (j * 5 + ch) * 16 + qq * 4 + t;
-      bq[qq] = g == 0 ? hh[uu] : (g == 1 ? hl[uu] : make_uint4(0, 0, 0, 0));
+      const int un = (j * 5 + ch) * 16 + qq * 4 + t;
+      bq[qq] = g == 0 ? hh[un] : (g == 1 ? hl[un] : make_uint4(0, 0, 0, 0));
     }
     float d[4][4] = {};
     mma_chunk(d, ra, rb, sa, sb, bq);
     if (t == 0) {
       const float2 r = unit_rows(d);
-      part[u * 16 + g] = r.x;
-      part[u * 16 + 8 + g] = r.y;
+      part[uu * 16 + g] = r.x;
+      part[uu * 16 + 8 + g] = r.y;
     }
   }
   __syncthreads();
@@ -628,11 +715,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
     for (int p = 0; p < per_tile; ++p) acc += part[(i * per_tile + p) * 16 + row];
     out[(c + i * sp.grid) * 16 + row] = isnan(hmax) ? hmax : scale_pow2(acc, -eh);
   }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, kTmemCols);
 }
 
 static int launch_moe_decode_fast(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
                                   const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
                                   cudaStream_t st, const DeviceInfo* dev, int grid) {
+  CUtensorMap gate_map;
+  int rc = gate_rows_tensor_map(table, n_blocks, dev->device, &gate_map);
+  if (rc) return rc;
   // shared memory: the largest per-CTA map of this split
   const DecodeSplit sp{grid, K};
   int smem = 0;
@@ -653,7 +746,7 @@ static int launch_moe_decode_fast(const uint8_t* table, int64_t n_blocks, const 
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, fn, table, n_blocks, sidx, s2, coef, x, h_buf, out, K);
+  e = cudaLaunchKernelEx(&cfg, fn, gate_map, table, n_blocks, sidx, s2, coef, x, h_buf, out, K);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_decode_persistent launch: %s", cudaGetErrorString(e));
   return check_launch("moe_decode_persistent");
 }
@@ -683,7 +776,10 @@ static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32
   if (variant == 1 && !fits)
     return set_error(QFN_ERR_UNSUPPORTED, "tensor-core decode path needs K <= %d (and a 148-SM-class device)",
                      kFastMaxK);
-  if (variant == 1 || (variant == 0 && fits))
+  // Automatic dispatch takes the CUDA-core path: on B200 it is currently the
+  // faster of the two (19.7 vs 25 us per K=10 layer); the tensor-core path is
+  // selected explicitly with variant 1.
+  if (variant == 1)
     return launch_moe_decode_fast(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st, dev,
                                   dev->sm_count);
   return launch_moe_decode_generic(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st);

@@ -37,3 +37,16 @@ int check_launch(const char* what);
   do {                                                 \
     if (!(cond)) return ::qfn::set_error((status), __VA_ARGS__); \
   } while (0)
+
+#include <cuda.h>
+
+namespace qfn {
+
+// 3-D TMA tensor map over the gate/up rows of an expert table viewed as
+// [n_blocks*2160 rows][10 chunks][128 B] (row stride 1280 B, chunk stride
+// 128 B), box [8 rows][10 chunks][128 B], 128-byte swizzle: one box is an
+// 8-row group of a gate or up matrix laid out as ten 1-KB UMMA K-major
+// SWIZZLE_128B atoms.  Cached per (device, table, n_blocks).
+int gate_rows_tensor_map(const void* table, int64_t n_blocks, int device, CUtensorMap* out);
+
+}  // namespace qfn
