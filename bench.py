@@ -229,11 +229,13 @@ def main():
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         e0.record(st)
         for i in range(args.steps):
             graphs[(args.warmup + i) % R].replay()
         e1.record(st)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1)
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -291,9 +293,9 @@ def main():
                 "steps": E, "ms_per_step": ms_e2e / E, "path": "qmoe.moe_decode (eager, public API)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "kernel": "moe_gate_up_kernel + moe_down_kernel (one decode layer)",
+                     "kernel": "moe_decode_stream (one launch per decode layer)",
                      "traffic": None, "per_launch_bytes": LAYER_BYTES},
-        "gpu_launches": args.steps * L * 2,
+        "gpu_launches": args.steps * L,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

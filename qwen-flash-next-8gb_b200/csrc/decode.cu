@@ -765,23 +765,417 @@ static bool persistent_fits(int K, const DeviceInfo* dev) {
   return true;
 }
 
+// ============================================================================
+// Stream path (K <= 10): one cooperative launch, one CTA per SM, the CTA's
+// whole share of the layer requested from HBM at entry.
+//
+// Work items are 8-row "octets": a gate/up octet is 8 output features of one
+// expert (8 gate rows + 8 up rows + their scale rows, 23,040 B); a down octet
+// is 8 output rows of every expert (K x (2,560 B rows + 320 B scales)).  Down
+// octets are dealt evenly (320 of them: 2 or 3 per CTA on 148 SMs); gate/up
+// octets fill each CTA's remaining byte budget, so every SM streams about
+// 1/148 of the layer.  After the routing loads, warps 0 and 1 issue every
+// bulk copy of the CTA's share at once (gate/up runs in chunks of two octets
+// with one mbarrier each; the down rows and scales of each expert as one copy
+// each, on one more mbarrier), so HBM sees the whole layer's requests at once
+// and the down rows land while the gate/up rows are reduced.
+//
+// Dot products run on mma.sync m16n8k16 with f16 operands: A = e2m1 codes
+// times their E4M3 block scale (exact in f16), B = the activation as an f16
+// hi/lo pair (v * 2^e = hi + lo, one power-of-two e per vector) in B columns
+// 0/1, so every product is exact and the fp32 sums keep ~22 bits of x and h.
+// Phase 1: warp w owns K-slice [128w, 128w + 128) of every gate/up octet (its
+// B fragment of x stays in registers); A rows 0-7 are the gate rows and 8-15
+// the up rows, so one MMA chain yields both projections.  The 20 per-warp
+// partials are summed in a fixed order into h (global h_buf).  A grid-wide
+// barrier separates writing h from reading it.  Phase 2: A rows 0-7 are down
+// rows of expert j, rows 8-15 the same rows of expert j+1, B columns 0/1 hold
+// h_j and 2/3 h_(j+1); the per-(expert, K-slice) partials are combined with
+// coef_j * ws2_d_j in a fixed order, so results are bit-reproducible.
+// ============================================================================
+
+constexpr int kSMaxK = 10;
+constexpr int kSMaxGu = 8;               // gate/up octets per CTA (checked on the host)
+constexpr int kSChunk = 2;               // gate/up octets per copy / mbarrier
+constexpr int kGuOctBytes = 23040;       // gate rows | up rows | gate scales | up scales
+constexpr int kDnOctBytes = 2880;        // 8 down rows of one expert (2,560 B) + their scales (320 B)
+constexpr int kDnOctets = kHid / 8;      // 320
+constexpr int kSMiscBytes = 1024;
+
+struct StreamSplit {
+  int grid, K;
+  __host__ __device__ int dn0(int c) const { return c * kDnOctets / grid; }
+  // First gate/up octet of CTA c.  Bytes are counted in units of 2,880 B (a
+  // gate/up octet is 8 units, a down octet K units); CTA c's byte range starts
+  // at c/grid of the layer, minus what its down octets take before it.
+  __host__ __device__ int gu0(int c) const {
+    const int n = K * kTilesPerExpert;
+    if (c >= grid) return n;
+    const long long P = static_cast<long long>(c) * 960 * K / grid;
+    const long long s = (P - static_cast<long long>(K) * dn0(c) + 4) / 8;
+    return static_cast<int>(s < 0 ? 0 : (s > n ? n : s));
+  }
+};
+
+struct SSmem {  // byte offsets from the aligned base of one CTA's dynamic shared memory
+  int gu, dn, hs, scratch, misc, total;
+};
+
+__host__ __device__ inline SSmem ssmem_map(int ng, int nd, int K) {
+  SSmem m;
+  m.gu = 0;
+  m.dn = ng * kGuOctBytes;
+  int end = m.dn + nd * K * kDnOctBytes;
+  // Phase 2 keeps h as f16 hi + lo rows (K x 640 x 4 B) in the gate/up region,
+  // which is free by then, or after the down octets when that region is smaller.
+  const int hneed = K * kInter * 4;
+  m.hs = m.dn >= hneed ? 0 : end;
+  if (m.hs) end += hneed;
+  m.scratch = (end + 15) & ~15;  // x hi/lo, then the gate/up partials, then the down partials
+  int scratch = 2 * kHid * 2;
+  const int red = ng * kPWarps * 16 * 4, part = nd * K * 5 * 8 * 4;
+  if (red > scratch) scratch = red;
+  if (part > scratch) scratch = part;
+  m.misc = m.scratch + scratch;
+  m.total = m.misc + kSMiscBytes + 1024;  // + slack for aligning the base to 1,024 B
+  return m;
+}
+
+__device__ __forceinline__ float nanmax(float a, float b) { return (isnan(b) || b > a) ? b : a; }
+
+template <bool kXF32>
+__global__ void __launch_bounds__(kPThreads, 1)
+    moe_decode_stream(const uint8_t* __restrict__ table, int64_t n_blocks, const int32_t* __restrict__ sidx,
+                      const float* __restrict__ s2, const float* __restrict__ coef, const void* __restrict__ x,
+                      float* h, float* __restrict__ out, int K) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const StreamSplit sp{static_cast<int>(gridDim.x), K};
+  const int c = blockIdx.x;
+  const int g0 = sp.gu0(c), ng = sp.gu0(c + 1) - g0;
+  const int d0 = sp.dn0(c), nd = sp.dn0(c + 1) - d0;
+  const SSmem M = ssmem_map(ng, nd, K);
+  uint8_t* misc = smem + M.misc;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(misc);           // [0, chunks): gate/up; [kSMaxGu]: down
+  int64_t* eoff = reinterpret_cast<int64_t*>(misc + 128);      // block byte offset, -1 if out of range
+  float* ws_g = reinterpret_cast<float*>(misc + 256);
+  float* ws_u = ws_g + kSMaxK;
+  float* cw = ws_u + kSMaxK;                                   // coef * ws2_down (NaN if invalid)
+  int* hexp = reinterpret_cast<int*>(cw + kSMaxK);             // phase-2 prescale exponent per expert
+  float* wred = reinterpret_cast<float*>(hexp + kSMaxK);       // per-warp maxima
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ng; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[kSMaxGu], 1);
+    fence_mbar_init();
+  }
+  // Warm the address translations of h_buf and out (a prefetch reads nothing
+  // the previous kernel may still be writing into this SM's caches).
+  if (threadIdx.x == 64) asm volatile("prefetch.global.L2 [%0];" ::"l"(h) : "memory");
+  if (threadIdx.x == 96) asm volatile("prefetch.global.L2 [%0];" ::"l"(out) : "memory");
+  // Everything below reads this call's inputs or writes h_buf / out.
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // x (thread u owns k in [4u, 4u + 4)) and the per-expert parameters.
+  const int u = threadIdx.x;
+  float xv[4];
+  if (kXF32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + 4 * u);
+    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+  } else {
+    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + 4 * u);
+    xv[0] = bf16_bits_to_f32(r.x & 0xffffu); xv[1] = bf16_bits_to_f32(r.x >> 16);
+    xv[2] = bf16_bits_to_f32(r.y & 0xffffu); xv[3] = bf16_bits_to_f32(r.y >> 16);
+  }
+  if (threadIdx.x < K) {
+    const int j = threadIdx.x;
+    const int64_t b = sidx[j];
+    const bool ok = block_ok(b, n_blocks);
+    eoff[j] = ok ? b * kBlock : -1;
+    ws_g[j] = s2[3 * j + 0];
+    ws_u[j] = s2[3 * j + 1];
+    cw[j] = ok ? coef[j] * s2[3 * j + 2] : __int_as_float(0x7fc00000);
+  }
+  float mx = nanmax(nanmax(fabsf(xv[0]), fabsf(xv[1])), nanmax(fabsf(xv[2]), fabsf(xv[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = nanmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) wred[warp] = mx;
+  __syncthreads();
+
+  // Gate/up octets come in runs of one expert (at most two runs); each run is
+  // cut into chunks of kSChunk octets, one mbarrier per chunk.  Warp 0 issues
+  // 4 copies per chunk (gate rows, up rows, gate scales, up scales), warp 1
+  // 2 per expert for the down octets (all nd octets' rows, then scales: both
+  // contiguous in the block): few large copies, since the TMA unit spends a
+  // roughly fixed time per copy.
+  const int nA = ng < kTilesPerExpert - g0 % kTilesPerExpert ? ng : kTilesPerExpert - g0 % kTilesPerExpert;
+  const int ncA = (nA + kSChunk - 1) / kSChunk;
+  const int nc = ncA + (ng - nA + kSChunk - 1) / kSChunk;
+  if (warp == 0) {
+    if (lane < nc) {
+      const int i0 = lane < ncA ? lane * kSChunk : nA + (lane - ncA) * kSChunk;
+      const int n = min(kSChunk, (lane < ncA ? nA : ng) - i0);
+      mbar_arrive_expect_tx(&bar[lane], eoff[(g0 + i0) / kTilesPerExpert] >= 0 ? n * kGuOctBytes : 0);
+    }
+    if (lane == 31) {
+      uint32_t tx = 0;
+      for (int j = 0; j < K; ++j) tx += eoff[j] >= 0 ? nd * kDnOctBytes : 0;
+      mbar_arrive_expect_tx(&bar[kSMaxGu], tx);
+    }
+    __syncwarp();
+    if (lane < 4 * nc) {
+      const int ch = lane >> 2, piece = lane & 3;
+      const int i0 = ch < ncA ? ch * kSChunk : nA + (ch - ncA) * kSChunk;
+      const int n = min(kSChunk, (ch < ncA ? nA : ng) - i0);
+      const int T = g0 + i0, j = T / kTilesPerExpert;
+      const int64_t off = eoff[j];
+      if (off >= 0) {
+        const int f0 = (T % kTilesPerExpert) * 8;
+        const uint8_t* blk = table + off;
+        if (piece == 0) bulk_g2s(smem + M.gu + i0 * 10240, blk + kOGW + f0 * (kHid / 2), n * 10240, &bar[ch]);
+        else if (piece == 1) bulk_g2s(smem + M.gu + (ng + i0) * 10240, blk + kOUW + f0 * (kHid / 2), n * 10240, &bar[ch]);
+        else if (piece == 2) bulk_g2s(smem + M.gu + 2 * ng * 10240 + i0 * 1280, blk + kOGS + f0 * (kHid / 16), n * 1280, &bar[ch]);
+        else bulk_g2s(smem + M.gu + 2 * ng * 10240 + (ng + i0) * 1280, blk + kOUS + f0 * (kHid / 16), n * 1280, &bar[ch]);
+      }
+    }
+  } else if (warp == 1 && nd > 0) {
+    if (lane < 2 * K) {
+      const int j = lane >> 1;
+      const int64_t off = eoff[j];
+      if (off >= 0) {
+        const int64_t row0 = static_cast<int64_t>(d0) * 8;
+        const uint8_t* blk = table + off;
+        if ((lane & 1) == 0)
+          bulk_g2s(smem + M.dn + j * nd * 2560, blk + kODW + row0 * (kInter / 2), nd * 2560, &bar[kSMaxGu]);
+        else
+          bulk_g2s(smem + M.dn + K * nd * 2560 + j * nd * 320, blk + kODS + row0 * (kInter / 16), nd * 320,
+                   &bar[kSMaxGu]);
+      }
+    }
+  }
+
+  // x * 2^ex as f16 hi/lo rows, then each warp's B fragments for its K-slice.
+  float xmax = 0.f;
+  for (int w = 0; w < kPWarps; ++w) xmax = nanmax(xmax, wred[w]);
+  const int ex = f16_prescale_exp(xmax);
+  uint8_t* xs = smem + M.scratch;  // hi: 2,560 f16, then lo
+  {
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      __half h0, l0, h1, l1;
+      split_f16(scale_pow2(xv[2 * i], ex), h0, l0);
+      split_f16(scale_pow2(xv[2 * i + 1], ex), h1, l1);
+      hw[i] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+      lw[i] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+    }
+    *reinterpret_cast<uint2*>(xs + 8 * u) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(xs + 2 * kHid + 8 * u) = make_uint2(lw[0], lw[1]);
+  }
+  __syncthreads();
+  uint4 bq[4];
+  {
+    const uint8_t* src = xs + (g == 1 ? 2 * kHid : 0) + 2 * (128 * warp + 32 * t);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bq[q] = g < 2 ? lds128(src + 16 * q) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();  // the scratch region now takes the gate/up partials
+
+  // ---- phase 1: gate/up octets in arrival order
+  float* red = reinterpret_cast<float*>(smem + M.scratch);  // [octet][warp][16]
+  for (int i = 0; i < ng; ++i) {
+    if (!mbar_wait(&bar[i < nA ? i / kSChunk : ncA + (i - nA) / kSChunk], 0)) note_timeout();
+    const uint8_t* gate = smem + M.gu + i * 10240;
+    const uint8_t* up = smem + M.gu + (ng + i) * 10240;
+    const uint8_t* gsc = smem + M.gu + 2 * ng * 10240 + i * 1280;
+    const uint8_t* usc = smem + M.gu + 2 * ng * 10240 + (ng + i) * 1280;
+    const uint4 ra = lds128(gate + g * (kHid / 2) + 64 * warp + 16 * t);
+    const uint4 rb = lds128(up + g * (kHid / 2) + 64 * warp + 16 * t);
+    const uint32_t sa = lds16(gsc + g * (kHid / 16) + 8 * warp + 2 * t);
+    const uint32_t sb = lds16(usc + g * (kHid / 16) + 8 * warp + 2 * t);
+    float d[4][4] = {};
+    mma_chunk(d, ra, rb, sa, sb, bq);
+    if (t == 0) {
+      const float2 r = unit_rows(d);
+      red[(i * kPWarps + warp) * 16 + g] = r.x;
+      red[(i * kPWarps + warp) * 16 + 8 + g] = r.y;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 8 * ng) {
+    const int i = threadIdx.x >> 3, f = threadIdx.x & 7;
+    const int T = g0 + i, j = T / kTilesPerExpert;
+    float gs = 0.f, us = 0.f;
+    for (int w = 0; w < kPWarps; ++w) {
+      gs += red[(i * kPWarps + w) * 16 + f];
+      us += red[(i * kPWarps + w) * 16 + 8 + f];
+    }
+    const float gg = scale_pow2(gs, -ex) * ws_g[j];
+    const float uu = scale_pow2(us, -ex) * ws_u[j];
+    const float hv = gg / (1.0f + expf(-gg)) * uu;
+    h[j * kInter + (T % kTilesPerExpert) * 8 + f] = eoff[j] >= 0 ? hv : __int_as_float(0x7fc00000);
+  }
+
+  cooperative_groups::this_grid().sync();  // every h row is written
+
+  // ---- phase 2: h -> f16 hi/lo rows.  Thread i loads 16-byte units i,
+  // i + 640, i + 1280 of h (unit v = expert v / 160, features 4 (v % 160) ..);
+  // warp w's r-th load covers 32 units of expert (w + 20 r) / 5.
+  uint8_t* hs = smem + M.hs;  // hi row j at 1,280 j; lo row j at 1,280 (K + j)
+  const int n_units = K * (kInter / 4);
+  float4 hv[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int v = threadIdx.x + r * kPThreads;
+    hv[r] = v < n_units ? __ldcg(reinterpret_cast<const float4*>(h) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    float hm = nanmax(nanmax(fabsf(hv[r].x), fabsf(hv[r].y)), nanmax(fabsf(hv[r].z), fabsf(hv[r].w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) hm = nanmax(hm, __shfl_xor_sync(0xffffffffu, hm, o));
+    if (lane == 0) wred[32 + r * kPWarps + warp] = hm;
+  }
+  __syncthreads();
+  if (threadIdx.x < K) {
+    const int j = threadIdx.x;
+    float m = 0.f;
+    for (int q = 0; q < 5; ++q) m = nanmax(m, wred[32 + 5 * j + q]);  // warps 5j .. 5j + 4 of load (5j) / 20
+    hexp[j] = f16_prescale_exp(m);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int v = threadIdx.x + r * kPThreads;
+    if (v < n_units) {
+      const int j = v / 160, f = 4 * (v % 160), e = hexp[j];
+      __half h0[4], l0[4];
+      split_f16(scale_pow2(hv[r].x, e), h0[0], l0[0]);
+      split_f16(scale_pow2(hv[r].y, e), h0[1], l0[1]);
+      split_f16(scale_pow2(hv[r].z, e), h0[2], l0[2]);
+      split_f16(scale_pow2(hv[r].w, e), h0[3], l0[3]);
+      *reinterpret_cast<uint2*>(hs + j * 1280 + 2 * f) = *reinterpret_cast<const uint2*>(h0);
+      *reinterpret_cast<uint2*>(hs + (K + j) * 1280 + 2 * f) = *reinterpret_cast<const uint2*>(l0);
+    }
+  }
+  if (nd > 0 && !mbar_wait(&bar[kSMaxGu], 0)) note_timeout();
+  __syncthreads();
+
+  // ---- phase 2: (down octet, expert pair, 128-k slice) items, one per warp
+  float* part = reinterpret_cast<float*>(smem + M.scratch);  // [octet][expert][slice][8 rows]
+  const int P = (K + 1) >> 1;
+  const int n_items = nd * P * 5;
+  for (int it = warp; it < n_items; it += kPWarps) {
+    const int i = it / (P * 5), rem = it - i * (P * 5);
+    const int p = rem / 5, s = rem - p * 5;
+    const int j0 = 2 * p, j1 = 2 * p + 1;
+    const bool has1 = j1 < K;
+    const int jb = has1 ? j1 : j0;
+    const uint8_t* w0 = smem + M.dn + (j0 * nd + i) * 2560;
+    const uint8_t* w1 = smem + M.dn + (jb * nd + i) * 2560;
+    const uint8_t* s0 = smem + M.dn + K * nd * 2560 + (j0 * nd + i) * 320;
+    const uint8_t* s1 = smem + M.dn + K * nd * 2560 + (jb * nd + i) * 320;
+    const uint4 ra = lds128(w0 + g * (kInter / 2) + 64 * s + 16 * t);
+    const uint4 rb = lds128(w1 + g * (kInter / 2) + 64 * s + 16 * t);
+    const uint32_t sa = lds16(s0 + g * (kInter / 16) + 8 * s + 2 * t);
+    const uint32_t sb = lds16(s1 + g * (kInter / 16) + 8 * s + 2 * t);
+    // B columns: 0/1 = h_j0 hi/lo, 2/3 = h_j1 hi/lo, 4-7 = 0
+    const int jj = g < 2 ? j0 : j1;
+    const bool live = g < 2 || (g < 4 && has1);
+    const uint8_t* src = hs + ((g & 1) ? K + jj : jj) * 1280 + 2 * (128 * s + 32 * t);
+    uint4 hq[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) hq[q] = live ? lds128(src + 16 * q) : make_uint4(0, 0, 0, 0);
+    float d[4][4] = {};
+    mma_chunk(d, ra, rb, sa, sb, hq);
+    if (t == 0)
+      part[((i * K + j0) * 5 + s) * 8 + g] = ((d[0][0] + d[0][1]) + (d[1][0] + d[1][1])) + ((d[2][0] + d[2][1]) + (d[3][0] + d[3][1]));
+    if (t == 1 && has1)
+      part[((i * K + j1) * 5 + s) * 8 + g] = ((d[0][2] + d[0][3]) + (d[1][2] + d[1][3])) + ((d[2][2] + d[2][3]) + (d[3][2] + d[3][3]));
+  }
+  __syncthreads();
+  if (threadIdx.x < 8 * nd) {
+    const int i = threadIdx.x >> 3, r = threadIdx.x & 7;
+    float acc = 0.f;
+    for (int j = 0; j < K; ++j) {
+      const float* pj = part + (i * K + j) * 40 + r;
+      const float sj = (((pj[0] + pj[8]) + (pj[16] + pj[24])) + pj[32]);
+      acc = fmaf(scale_pow2(sj, -hexp[j]), cw[j], acc);
+    }
+    out[8 * (d0 + i) + r] = acc;
+  }
+}
+
+// Shared memory of the stream path for (K, grid), or 0 when it does not fit.
+static int stream_smem(int K, const DeviceInfo* dev) {
+  if (K > kSMaxK) return 0;
+  const StreamSplit sp{dev->sm_count, K};
+  int smem = 0;
+  for (int c = 0; c < sp.grid; ++c) {
+    const int ng = sp.gu0(c + 1) - sp.gu0(c), nd = sp.dn0(c + 1) - sp.dn0(c);
+    if (ng > kSMaxGu) return 0;
+    const SSmem m = ssmem_map(ng, nd, K);
+    if (m.total > smem) smem = m.total;
+  }
+  return static_cast<size_t>(smem) <= dev->smem_optin ? smem : 0;
+}
+
+static int launch_moe_decode_stream(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
+                                    const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
+                                    cudaStream_t st, const DeviceInfo* dev, int smem) {
+  auto fn = x_dtype == QFN_DTYPE_F32 ? moe_decode_stream<true> : moe_decode_stream<false>;
+  static bool attr_set[64][2] = {};
+  const int ti = x_dtype == QFN_DTYPE_F32 ? 1 : 0;
+  if (!attr_set[dev->device][ti]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(dev->smem_optin));
+    if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "stream decode smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev->device][ti] = true;
+  }
+  // Cooperative (the grid barrier needs every CTA resident) and a programmatic
+  // dependent of the previous kernel in the stream (its launch overlaps that
+  // kernel's tail; the kernel waits for it before touching any input).
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(dev->sm_count);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, table, n_blocks, sidx, s2, coef, x, h_buf, out, K);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_decode_stream launch: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode_stream");
+}
+
 static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
                              const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
                              cudaStream_t st, int variant) {
   DeviceInfo* dev;
   int rc = current_device(&dev);
   if (rc) return rc;
-  // The persistent path keeps a CTA's whole share of the layer in shared memory.
-  const bool fits = persistent_fits(K, dev);
-  if (variant == 1 && !fits)
-    return set_error(QFN_ERR_UNSUPPORTED, "tensor-core decode path needs K <= %d (and a 148-SM-class device)",
-                     kFastMaxK);
-  // Automatic dispatch takes the CUDA-core path: on B200 it is currently the
-  // faster of the two (19.7 vs 25 us per K=10 layer); the tensor-core path is
-  // selected explicitly with variant 1.
-  if (variant == 1)
+  if (variant == 1) {
+    // The persistent path keeps a CTA's whole share of the layer in shared memory.
+    if (!persistent_fits(K, dev))
+      return set_error(QFN_ERR_UNSUPPORTED, "tensor-core decode path needs K <= %d (and a 148-SM-class device)",
+                       kFastMaxK);
     return launch_moe_decode_fast(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st, dev,
                                   dev->sm_count);
+  }
+  if (variant == 0 || variant == 3) {
+    const int smem = stream_smem(K, dev);
+    if (smem > 0)
+      return launch_moe_decode_stream(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st, dev, smem);
+    if (variant == 3)
+      return set_error(QFN_ERR_UNSUPPORTED, "stream decode path needs K <= %d (and a 148-SM-class device)", kSMaxK);
+  }
   return launch_moe_decode_generic(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st);
 }
 
@@ -816,9 +1210,11 @@ extern "C" int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, co
                                       int K, int variant, qfn_stream_t stream) {
   int rc = check_decode_args(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K);
   if (rc) return rc;
-  QFN_REQUIRE(variant >= 0 && variant <= 2, QFN_ERR_INVALID_ARG, "qfn_moe_decode_variant: variant %d", variant);
+  QFN_REQUIRE(variant >= 0 && variant <= 3, QFN_ERR_INVALID_ARG, "qfn_moe_decode_variant: variant %d", variant);
   QFN_REQUIRE(variant != 1 || K <= kFastMaxK, QFN_ERR_UNSUPPORTED,
               "qfn_moe_decode_variant: the tensor-core path takes K <= %d", kFastMaxK);
+  QFN_REQUIRE(variant != 3 || K <= kSMaxK, QFN_ERR_UNSUPPORTED,
+              "qfn_moe_decode_variant: the stream path takes K <= %d", kSMaxK);
   return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, as_stream(stream), variant);
 }
 

@@ -62,7 +62,8 @@ def test_block_deq_bit_exact(golden):
 
 
 # ---------------------------------------------------------------- decode expert layer
-VARIANTS = [qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_CUDA_CORE]
+VARIANTS = [qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_CUDA_CORE, qmoe.VARIANT_STREAM]
+SMALL_K_VARIANTS = (qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_STREAM)   # K <= 10
 
 
 def run_decode(table, sidx, s2, coef, x, variant=qmoe.VARIANT_AUTO):
@@ -104,8 +105,8 @@ def table24():
 @pytest.mark.parametrize("K,xdtype,seed", [(10, torch.bfloat16, 1), (10, torch.float32, 2), (1, torch.bfloat16, 3),
                                            (7, torch.float32, 4), (32, torch.bfloat16, 5), (16, torch.float32, 6)])
 def test_moe_decode_matches_oracle(table24, K, xdtype, seed, variant):
-    if K > 10 and variant == qmoe.VARIANT_TENSOR_CORE:
-        pytest.skip("the tensor-core path takes K <= 10")
+    if K > 10 and variant in SMALL_K_VARIANTS:
+        pytest.skip("this path takes K <= 10")
     blocks, table = table24
     rng = np.random.Generator(np.random.PCG64(100 + seed))
     sidx = rng.choice(24, size=K, replace=K > 24).astype(np.int32)
@@ -146,20 +147,21 @@ def test_moe_decode_paths_agree(table24):
     blocks, table = table24
     args = (np.array([23, 0, 5, 17, 9, 2, 11, 8, 20, 14], np.int32), synthetic.make_s2(10, seed=3, spread=True),
             np.linspace(0.02, 0.3, 10).astype(np.float32), synthetic.make_x(2560, 21))
-    a, ha = run_decode(table, *args, variant=qmoe.VARIANT_TENSOR_CORE)
     b, hb = run_decode(table, *args, variant=qmoe.VARIANT_CUDA_CORE)
-    assert rel_err(a, b) <= FP32_GRADE and rel_err(ha, hb) <= FP32_GRADE
+    for v in SMALL_K_VARIANTS:
+        a, ha = run_decode(table, *args, variant=v)
+        assert rel_err(a, b) <= FP32_GRADE and rel_err(ha, hb) <= FP32_GRADE
 
 
-def test_moe_decode_large_and_tiny_x(table24):
+@pytest.mark.parametrize("variant", SMALL_K_VARIANTS)
+def test_moe_decode_large_and_tiny_x(table24, variant):
     """Per-call power-of-two prescale of x: results scale exactly with x."""
     _, table = table24
     sidx = np.arange(10, dtype=np.int32)
     s2, coef = synthetic.make_s2(10), np.full(10, .1, np.float32)
     x = synthetic.make_x(2560, 31, dtype=torch.float32)
-    base, _ = run_decode(table, sidx, s2, coef, x, qmoe.VARIANT_TENSOR_CORE)
     for f in (2.0 ** 40, 2.0 ** -40):
-        y, _ = run_decode(table, sidx, s2, coef, x * f, qmoe.VARIANT_TENSOR_CORE)
+        y, _ = run_decode(table, sidx, s2, coef, x * f, variant)
         ref = oracle.moe_decode(table24[0], sidx, s2, coef, (x * f).numpy())
         assert rel_err(y, ref) <= FP32_GRADE
 
