@@ -165,6 +165,42 @@ int qfn_device_status(unsigned int* status, int clear);
 int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
                   int y_dtype, int64_t N, int64_t K, qfn_stream_t stream);
 
+/*
+ * qfn_moe_prefill -- the batched-prefill expert loop of QwenEngine.moe
+ * (qwen_engine.py:835-852), which the reference runs as a Python loop over
+ * experts (block_deq + three fp32 torch GEMMs + index_add_ per expert):
+ *   out[t] = sum_k tv[t][k] * down_e(silu(gate_e x[t]) * up_e x[t]),
+ *   e = ti[t][k], expert e's block at table[(base + e) * QFN_BLOCK_BYTES].
+ *   x:     bf16[T][2560] device, 16-byte aligned.
+ *   ti:    [T][topk] device expert ids in [0, n_experts), int64 (torch.topk's
+ *          output; ti_is_int64 = 1) or int32.  Pairs with an id outside the
+ *          range are skipped and flagged in qfn_prefill_status (bit 2).
+ *   tv:    [T][topk] device routing weights, tv_dtype BF16 or F32.
+ *   s2l:   f32[n_experts][3] device (ws2 gate/up/down of the layer's experts).
+ *   out:   f32[T][2560] device, 16-byte aligned; written (not accumulated).
+ *   workspace: device scratch of qfn_moe_prefill_workspace(T, topk,
+ *          n_experts) bytes, 256-byte aligned.
+ *   1 <= topk <= QFN_MAX_TOPK, 1 <= n_experts <= 1024, base + n_experts <=
+ *   n_blocks.  Six launches on `stream` (routing sort, activation gather,
+ *   tcgen05 gate/up GEMM, h packing, zeroing of out, tcgen05 down GEMM).
+ *   The combine adds with fp32 atomics, so the summation order over a
+ *   token's experts varies between calls (as index_add_ on CUDA).
+ */
+size_t qfn_moe_prefill_workspace(int64_t T, int topk, int n_experts);
+int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_is_int64,
+                    const void* tv, int tv_dtype, int topk, const uint8_t* table,
+                    int64_t n_blocks, int64_t base, const float* s2l, int n_experts,
+                    float* out, void* workspace, size_t workspace_bytes,
+                    qfn_stream_t stream);
+
+/*
+ * qfn_prefill_status -- read (and with clear != 0 reset) the prefill status
+ * word of the current device: bit 0 = a bounded wait ran out (outputs of that
+ * call invalid), bit 2 = an expert id outside [0, n_experts) was skipped.
+ * No counterpart in the reference.
+ */
+int qfn_prefill_status(unsigned int* status, int clear);
+
 #ifdef __cplusplus
 }
 #endif

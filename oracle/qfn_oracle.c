@@ -213,15 +213,15 @@ void oracle_moe_prefill(const float* x, long T, const int32_t* ti, const float* 
         H[i * INTER + n] = silu((float)ag) * (float)au;
       }
     }
-    /* index_add_: contributions of expert e land in token order; rows of
-     * distinct tokens never collide (one slot per expert per token). */
+    /* index_add_: contributions of expert e land in pair order.  Threads own
+     * output columns r, so a token routed to e twice accumulates without a
+     * race, in the same order as torch's CPU index_add_. */
 #pragma omp parallel for schedule(static)
-    for (long i = 0; i < m; ++i) {
-      float* orow = out + tok[i] * HID;
-      for (long r = 0; r < HID; ++r) {
+    for (long r = 0; r < HID; ++r) {
+      for (long i = 0; i < m; ++i) {
         double a = 0.0;
         for (long n = 0; n < INTER; ++n) a += (double)H[i * INTER + n] * D[r * INTER + n];
-        orow[r] += (float)a * w[i];
+        out[tok[i] * HID + r] += (float)a * w[i];
       }
     }
   }

@@ -28,7 +28,12 @@ SIGNATURES = {
     "qfn_moe_decode_noalloc": [_P, _I64, _P, _P, _P, _P, _I, _P, _I, _P],
     "qfn_device_status": [_P, _I],
     "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
+    "qfn_moe_prefill_workspace": [_I64, _I, _I],
+    "qfn_moe_prefill": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P],
+    "qfn_prefill_status": [_P, _I],
 }
+# entry points whose return value is not an int status
+RESTYPES = {"qfn_moe_prefill_workspace": ctypes.c_size_t}
 
 
 class QfnError(RuntimeError):
@@ -53,7 +58,7 @@ def lib():
         for name, argtypes in SIGNATURES.items():
             fn = getattr(L, name)
             fn.argtypes = argtypes
-            fn.restype = _I
+            fn.restype = RESTYPES.get(name, _I)
         _lib = L
     return _lib
 
@@ -68,6 +73,13 @@ def device_status(clear=True):
     """Device status word of the current device (bit 0: a kernel wait timed out)."""
     v = ctypes.c_uint(0)
     check(lib().qfn_device_status(ctypes.byref(v), int(clear)), "qfn_device_status")
+    return v.value
+
+
+def prefill_status(clear=True):
+    """Prefill status word of the current device (bit 0: a wait timed out; bit 2: bad expert id skipped)."""
+    v = ctypes.c_uint(0)
+    check(lib().qfn_prefill_status(ctypes.byref(v), int(clear)), "qfn_prefill_status")
     return v.value
 
 

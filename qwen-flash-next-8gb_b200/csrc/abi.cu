@@ -137,3 +137,66 @@ int gate_rows_tensor_map(const void* table, int64_t n_blocks, int device, CUtens
 }
 
 }  // namespace qfn
+
+// ---------------------------------------------------------------------------
+// Generic 2-D tensor-map cache
+namespace {
+struct Tmap2Entry {
+  const void* base;
+  int dtype, device, swizzle;
+  uint64_t inner, rows, stride;
+  uint32_t box_inner, box_rows;
+  CUtensorMap map;
+};
+constexpr int kTmap2Slots = 64;
+Tmap2Entry g_tmaps2[kTmap2Slots];
+int g_tmap2_count = 0, g_tmap2_next = 0;
+}  // namespace
+
+namespace qfn {
+
+int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t rows,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle,
+                  int device, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  for (int i = 0; i < g_tmap2_count; ++i) {
+    const Tmap2Entry& t = g_tmaps2[i];
+    if (t.base == base && t.dtype == static_cast<int>(dtype) && t.device == device &&
+        t.swizzle == static_cast<int>(swizzle) && t.inner == inner && t.rows == rows && t.stride == row_stride_bytes &&
+        t.box_inner == box_inner && t.box_rows == box_rows) {
+      *out = t.map;
+      return QFN_OK;
+    }
+  }
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || !fn) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled (2-D) failed (%d)", static_cast<int>(r));
+  Tmap2Entry& t = g_tmaps2[g_tmap2_count < kTmap2Slots ? g_tmap2_count++ : (g_tmap2_next++ % kTmap2Slots)];
+  t.base = base;
+  t.dtype = static_cast<int>(dtype);
+  t.device = device;
+  t.swizzle = static_cast<int>(swizzle);
+  t.inner = inner;
+  t.rows = rows;
+  t.stride = row_stride_bytes;
+  t.box_inner = box_inner;
+  t.box_rows = box_rows;
+  t.map = m;
+  *out = m;
+  return QFN_OK;
+}
+
+}  // namespace qfn
+

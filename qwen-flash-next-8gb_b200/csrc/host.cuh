@@ -49,4 +49,10 @@ namespace qfn {
 // SWIZZLE_128B atoms.  Cached per (device, table, n_blocks).
 int gate_rows_tensor_map(const void* table, int64_t n_blocks, int device, CUtensorMap* out);
 
+// 2-D TMA tensor map over `rows` rows of `inner` elements (row stride in
+// bytes), box [box_rows][box_inner], cached per (device, all arguments).
+int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t rows,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle,
+                  int device, CUtensorMap* out);
+
 }  // namespace qfn

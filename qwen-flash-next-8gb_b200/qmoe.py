@@ -81,6 +81,56 @@ def _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant):
     return out
 
 
+def moe_prefill(x, ti, tv, table, s2, L=0):
+    """Batched-prefill MoE experts of one layer (the loop at qwen_engine.py:835-852).
+
+    x bf16[T, 2560] . ti int64/int32[T, topk] expert ids of the layer . tv
+    bf16/fp32[T, topk] routing weights . table u8[NB, BLOCK] (the HBM-resident
+    expert table; expert e of layer L is block L * n_experts + e) . s2
+    f32[n_experts, 3] ws2 of the layer's experts (store.s2[L]) -> new fp32
+    [T, 2560] = sum_k tv[t,k] * down_e(silu(gate_e x_t) * up_e x_t), the
+    reference's `out` before its cast to bf16.  One call replaces the whole
+    per-expert loop (and its host syncs): grouped tcgen05 GEMMs on the GPU.
+    Queued on torch's current stream; graph-capturable.
+    """
+    require_cuda("x", x, torch.bfloat16)
+    require_cuda("ti", ti)
+    require_cuda("tv", tv)
+    require_cuda("table", table, torch.uint8)
+    require_cuda("s2", s2, torch.float32)
+    if x.dim() != 2 or x.shape[1] != HID:
+        raise ValueError(f"x must be bf16[T, {HID}], got {tuple(x.shape)}")
+    T = x.shape[0]
+    if ti.dim() != 2 or ti.shape[0] != T or tuple(tv.shape) != tuple(ti.shape):
+        raise ValueError(f"ti and tv must be [T, topk] with T={T}; got {tuple(ti.shape)}, {tuple(tv.shape)}")
+    if ti.dtype not in (torch.int64, torch.int32):
+        raise TypeError("ti must be int64 or int32")
+    if tv.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("tv must be bf16 or fp32")
+    if s2.dim() != 2 or s2.shape[1] != 3:
+        raise ValueError(f"s2 must be f32[n_experts, 3], got {tuple(s2.shape)}")
+    if table.dim() != 2 or table.shape[1] != BLOCK:
+        raise ValueError(f"table must be [NB, {BLOCK}]")
+    dev = x.device
+    for name, t in (("ti", ti), ("tv", tv), ("table", table), ("s2", s2)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, x on {dev}")
+    topk, E = ti.shape[1], s2.shape[0]
+    out = torch.empty(T, HID, dtype=torch.float32, device=dev)
+    if T == 0:
+        return out
+    L_ = lib()
+    nbytes = L_.qfn_moe_prefill_workspace(T, topk, E)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = L_.qfn_moe_prefill(x.data_ptr(), T, ti.data_ptr(), int(ti.dtype == torch.int64), tv.data_ptr(),
+                                DTYPE_BF16 if tv.dtype == torch.bfloat16 else DTYPE_F32, topk, table.data_ptr(),
+                                table.shape[0], int(L) * E, s2.data_ptr(), E, out.data_ptr(), ws.data_ptr(),
+                                nbytes, stream_of(out))
+    check(rc, "qfn_moe_prefill")
+    return out
+
+
 def deq(w_u8, s_e4m3_u8, ws2):
     """w_u8 [N, K/2] . s [N, K/16] (E4M3 bytes) . ws2 -> fp32 [N, K] (qmoe.py:93-102), on the GPU."""
     if SWAP:

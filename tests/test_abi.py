@@ -107,3 +107,31 @@ def test_reference_constants_kept():
     # the block layout adds up (repack_experts.py:12-19)
     sizes = [819200] * 3 + [102400] * 3
     assert sum(sizes) == qmoe.BLOCK and qmoe.BLOCK % 4096 == 0
+
+
+def test_prefill_validation_and_workspace_size():
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x10000)
+    T, topk, E = 2048, 10, 512
+    P = T * topk
+    ws = lib.qfn_moe_prefill_workspace(T, topk, E)
+    # pair arrays + f16 x rows + fp32 h + f16 hi/lo h dominate
+    assert ws >= P * (2560 * 2 + 640 * 4 + 640 * 4)
+    assert lib.qfn_moe_prefill_workspace(0, topk, E) == 0
+    args = dict(x=fake, T=T, ti=fake, i64=1, tv=fake, tvd=1, topk=topk, table=fake, nb=24576, base=0, s2=fake,
+                E=E, out=fake, ws=fake, wsb=ws)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return lib.qfn_moe_prefill(a["x"], a["T"], a["ti"], a["i64"], a["tv"], a["tvd"], a["topk"], a["table"],
+                                   a["nb"], a["base"], a["s2"], a["E"], a["out"], a["ws"], a["wsb"], None)
+
+    assert call(T=0) == 0                        # nothing to do
+    assert call(x=None) == 1                     # null pointer
+    assert call(topk=33) == 1                    # topk outside [1, 32]
+    assert call(E=1025) == 4                     # more experts than the routing kernel holds
+    assert call(tvd=7) == 1                      # unknown tv dtype
+    assert call(base=24576 - 100) == 1           # layer's experts past the end of the table
+    assert call(wsb=ws - 1) == 5                 # workspace too small
+    assert call(ws=ctypes.c_void_p(0x10010)) == 2  # workspace not 256-byte aligned
+

@@ -1,0 +1,155 @@
+"""GPU parity of the batched-prefill grouped expert GEMM (qmoe.moe_prefill,
+the C ABI's qfn_moe_prefill) against the reference's golden vector for the
+expert loop of qwen_engine.py:835-852 and against the CPU oracle.
+
+Tolerance: the contract is max|cand - ref| <= 1e-3 * RMS(ref) (TOL).  The
+kernels multiply exactly (bf16 x and e2m1 x E4M3 weights are exact in f16;
+h enters the down GEMM as an f16 hi/lo pair) and accumulate in the tensor
+cores' fp32 accumulators over K = 2560 and 2 x 640, so they are held to
+PREFILL_GRADE = 1e-4, ten times inside the contract (measured: <= 6e-5).
+The combine uses fp32 atomics (as index_add_ does on CUDA), so two calls
+agree to PREFILL_GRADE, not bit for bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+import _lib
+import oracle
+import qmoe
+import routing
+import synthetic
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+PREFILL_GRADE = 1e-4
+DEV = "cuda"
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+@pytest.fixture(autouse=True)
+def prefill_status_clean():
+    _lib.prefill_status(clear=True)
+    yield
+    assert _lib.prefill_status(clear=True) & 1 == 0, "a bounded wait in the prefill kernels ran out"
+
+
+def run(x, ti, tv, table, s2l, L=0, ti_dtype=torch.int64, tv_dtype=torch.float32):
+    out = qmoe.moe_prefill(x.to(DEV), cuda(ti).to(ti_dtype), cuda(tv).to(tv_dtype), table, cuda(s2l), L)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_prefill_matches_reference_golden(golden):
+    c = golden.cases["prefill_t8"]
+    T, E = c["T"], c["experts"]
+    table = cuda(synthetic.make_blocks(E, seed=c["table_seed"]))
+    s2l = synthetic.make_s2(E, seed=c["s2_seed"], spread=True)
+    x = synthetic.make_x(T * 2560, seed=c["x_seed"]).view(T, 2560)
+    ti, coef = golden.load("prefill_t8_ti"), golden.load("prefill_t8_coef")
+    ref = golden.load("prefill_t8_out")
+    for ti_dtype in (torch.int64, torch.int32):
+        for tv_dtype in (torch.float32, torch.bfloat16):   # coef holds bf16 values: exact in both
+            out = run(x, ti, coef, table, s2l, ti_dtype=ti_dtype, tv_dtype=tv_dtype)
+            assert rel_err(out, ref) <= PREFILL_GRADE
+            assert (np.argmax(out, axis=1) == np.argmax(ref, axis=1)).all()
+
+
+@pytest.fixture(scope="module")
+def table64():
+    blocks = synthetic.make_blocks(128, seed=7)        # two "layers" of 64 experts
+    return blocks, cuda(blocks)
+
+
+@pytest.mark.parametrize("T,topk,L,seed", [(1, 2, 0, 1), (40, 4, 1, 2), (150, 10, 0, 3), (97, 6, 1, 4)])
+def test_prefill_matches_oracle(table64, T, topk, L, seed):
+    blocks, table = table64
+    E = 64
+    s2l = synthetic.make_s2(E, seed=10 + seed, spread=True)
+    x = synthetic.make_x(T * 2560, seed=20 + seed).view(T, 2560)
+    ti, coef = oracle.route(synthetic.zipf_logits(T, seed=30 + seed, n_experts=E), topk)
+    out = run(x, ti, coef, table, s2l, L=L)
+    ref = oracle.moe_prefill(x.float().numpy(), ti, coef, blocks, L * E, s2l)
+    assert rel_err(out, ref) <= PREFILL_GRADE
+    assert (np.argmax(out, axis=1) == np.argmax(ref, axis=1)).all()
+
+
+def test_prefill_expert_with_several_tiles(table64):
+    """One expert receives 300 pairs (tiles of 128, 128, 44); the rest are spread."""
+    blocks, table = table64
+    E, T, topk = 64, 300, 3
+    rng = np.random.Generator(np.random.PCG64(5))
+    ti = np.stack([np.full(T, 17), (np.arange(T) % 63 + 18) % 64,
+                   rng.integers(0, 17, T)], axis=1).astype(np.int32)
+    coef = rng.random((T, topk)).astype(np.float32)
+    s2l = synthetic.make_s2(E, seed=6, spread=True)
+    x = synthetic.make_x(T * 2560, seed=7).view(T, 2560)
+    out = run(x, ti, coef, table, s2l)
+    ref = oracle.moe_prefill(x.float().numpy(), ti, coef, blocks, 0, s2l)
+    assert rel_err(out, ref) <= PREFILL_GRADE
+
+
+def test_prefill_skips_and_flags_out_of_range_experts(table64):
+    blocks, table = table64
+    E, T, topk = 64, 20, 4
+    s2l = synthetic.make_s2(E, seed=8)
+    x = synthetic.make_x(T * 2560, seed=9).view(T, 2560)
+    ti, coef = oracle.route(synthetic.zipf_logits(T, seed=10, n_experts=E), topk)
+    ti[3, 1], ti[7, 0] = 64, -1                       # outside [0, 64): skipped like the reference loop
+    out = run(x, ti, coef, table, s2l)
+    assert _lib.prefill_status(clear=True) & 4
+    ref = oracle.moe_prefill(x.float().numpy(), ti, coef, blocks, 0, s2l)
+    assert rel_err(out, ref) <= PREFILL_GRADE
+
+
+def test_prefill_large_and_tiny_activations(table64):
+    """Per-token power-of-two scaling of x: results follow x over a wide range."""
+    blocks, table = table64
+    E, T, topk = 64, 16, 4
+    s2l = synthetic.make_s2(E, seed=11)
+    ti, coef = oracle.route(synthetic.zipf_logits(T, seed=12, n_experts=E), topk)
+    x = synthetic.make_x(T * 2560, seed=13, dtype=torch.float32).view(T, 2560)
+    for f in (2.0 ** 30, 2.0 ** -30):
+        xs = (x * f).to(torch.bfloat16)
+        out = run(xs, ti, coef, table, s2l)
+        ref = oracle.moe_prefill(xs.float().numpy(), ti, coef, blocks, 0, s2l)
+        assert rel_err(out, ref) <= PREFILL_GRADE
+
+
+def test_prefill_graph_capture_and_repeat(table64):
+    blocks, table = table64
+    E, T, topk = 64, 64, 10
+    s2l = cuda(synthetic.make_s2(E, seed=14, spread=True))
+    x = synthetic.make_x(T * 2560, seed=15).view(T, 2560).to(DEV)
+    ti_np, coef_np = oracle.route(synthetic.zipf_logits(T, seed=16, n_experts=E), topk)
+    ti, tv = cuda(ti_np).long(), cuda(coef_np).to(torch.bfloat16)
+    first = qmoe.moe_prefill(x, ti, tv, table, s2l)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = qmoe.moe_prefill(x, ti, tv, table, s2l)
+    g.replay()
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), first.cpu().numpy()) <= PREFILL_GRADE
+    ref = oracle.moe_prefill(x.float().cpu().numpy(), ti_np, coef_np, blocks, 0, s2l.cpu().numpy())
+    assert rel_err(y.cpu().numpy(), ref) <= PREFILL_GRADE
+
+
+def test_prefill_routing_on_device_end_to_end(table64):
+    """Router on the GPU (routing.route) feeding moe_prefill, as QwenEngine.moe does."""
+    blocks, table = table64
+    E, T, topk = 64, 33, 10
+    logits = synthetic.zipf_logits(T, seed=17, n_experts=E)
+    ti, tv = routing.route(cuda(logits), topk)
+    s2l = synthetic.make_s2(E, seed=18, spread=True)
+    x = synthetic.make_x(T * 2560, seed=19).view(T, 2560)
+    out = qmoe.moe_prefill(x.to(DEV), ti, tv, table, cuda(s2l)).cpu().numpy()
+    ti_ref, coef_ref = oracle.route(logits, topk)
+    assert np.array_equal(ti.cpu().numpy(), ti_ref)
+    ref = oracle.moe_prefill(x.float().numpy(), ti_ref, coef_ref, blocks, 0, s2l)
+    assert rel_err(out, ref) <= PREFILL_GRADE
