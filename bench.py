@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--cpu-layers", type=int, default=4, help="layers timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                   help="decode: config 2 (default, the headline line); prefill: config 3")
+    p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
+    p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
     return p.parse_args()
 
 
@@ -177,12 +181,169 @@ def build_workload(args, dev):
     return table, sidx, s2, coef, x
 
 
+# ---------------------------------------------------------------- prefill (config 3)
+PF_TOPK = 10
+PF_FLOP_PER_PAIR = 2 * 3 * INTER * HID          # gate, up and down: 9,830,400 FLOP per (token, expert)
+PF_METRIC = "prefill tokens/s (one NVFP4 MoE layer: top-10 of 512 experts, Zipf(1.1) popularity)"
+
+
+def prefill_inputs(args, dev, R):
+    """R routed steps of config 3: x bf16 [T, 2560] ~ N(0,1); fp32 logits = log p[perm] + Gumbel with
+    p_r ~ r^-1.1 (one popularity permutation), top-10 + renormalised bf16 weights (the engine's router)."""
+    import torch
+    import routing
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 7)
+    T = args.tokens
+    logp = -1.1 * torch.log(torch.arange(1, N_EXPERTS + 1, device=dev, dtype=torch.float64))
+    logp = (logp - torch.logsumexp(logp, 0)).float()
+    perm = torch.randperm(N_EXPERTS, device=dev, generator=g)
+    xs, tis, tvs = [], [], []
+    for _ in range(R):
+        u = torch.rand(T, N_EXPERTS, device=dev, generator=g).clamp_(1e-12, 1 - 1e-7)
+        ti, tv = routing.route(logp[perm][None] - torch.log(-torch.log(u)), PF_TOPK)
+        xs.append(torch.randn(T, HID, device=dev, generator=g).to(torch.bfloat16))
+        tis.append(ti)
+        tvs.append(tv)
+    return xs, tis, tvs
+
+
+def run_prefill(args, rank, world):
+    import torch
+    import qmoe
+    from expert_table import ExpertTable
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        raise SystemExit("bench.py --workload prefill runs on one GPU (expert-parallel prefill: see --gpus 1)")
+    table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=N_EXPERTS)
+    table.fill_synthetic(seed=args.seed)
+    s2 = table.s2[0].contiguous()
+    R = 4
+    xs, tis, tvs = prefill_inputs(args, dev, R)
+    T = args.tokens
+    pairs = T * PF_TOPK
+    distinct = [int(torch.unique(t).numel()) for t in tis]
+    layer_bytes = [d * BLOCK + T * HID * 2 + T * HID * 4 for d in distinct]
+
+    def step(i):
+        return qmoe.moe_prefill(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(st)
+        for i in range(args.steps):
+            step(i)
+        e1.record(st)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    ms = e0.elapsed_time(e1) / args.steps
+    tok_s = T / (ms * 1e-3)
+    tflops = pairs * PF_FLOP_PER_PAIR / (ms * 1e-3) / 1e12
+    avg_bytes = sum(layer_bytes[i % R] for i in range(args.steps)) / args.steps
+    gbs = avg_bytes / (ms * 1e-3) / 1e9
+
+    # e2e: host buffers in (x, ti, tv) and the fp32 result out, every step
+    h_x = [x.cpu().pin_memory() for x in xs]
+    h_ti = [t.cpu().pin_memory() for t in tis]
+    h_tv = [t.cpu().pin_memory() for t in tvs]
+    h_out = torch.empty(T, HID, dtype=torch.float32).pin_memory()
+    d_x, d_ti, d_tv = torch.empty_like(xs[0]), torch.empty_like(tis[0]), torch.empty_like(tvs[0])
+    h2d = d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2
+    d2h = T * HID * 4
+
+    def e2e_step(i):
+        d_x.copy_(h_x[i % R], non_blocking=True)
+        d_ti.copy_(h_ti[i % R], non_blocking=True)
+        d_tv.copy_(h_tv[i % R], non_blocking=True)
+        y = qmoe.moe_prefill(d_x, d_ti, d_tv, table.slots, s2, 0)
+        h_out.copy_(y, non_blocking=True)
+
+    E = min(args.e2e_steps, args.steps)
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(E):
+        e2e_step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / E
+
+    tc_peak, tc_kind = tensor_peak()
+    line = {
+        "metric": PF_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, "
+                                      "fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"prefill-moe-1L (config 3): {T} tokens, top-{PF_TOPK} of {N_EXPERTS}, Zipf(1.1), "
+                               f"{pairs} pairs, {sum(distinct) / R:.0f} distinct experts per step",
+                   "tflops": tflops, "hbm_gbs": gbs, "bytes_per_step": avg_bytes,
+                   "flop_per_step": pairs * PF_FLOP_PER_PAIR,
+                   "l2": "no flush: each step reads >= 1.4 GB of distinct expert blocks (> 126 MB L2)",
+                   "parallelism": "single GPU"},
+        "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
+                "path": "qmoe.moe_prefill (public API) with pinned host inputs and output"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": tflops / tc_peak, "peak_kind": tc_kind,
+                     "hbm_frac": gbs / peaks()[0], "traffic": None,
+                     "kernel": "pf_gemm<gate/up> + pf_gemm<down> (+ routing, gather, h packing)"},
+        "gpu_launches": args.steps * 6,
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = prefill_cpu_baseline(args, table, s2, xs[0], tis[0], tvs[0])
+    print(json.dumps(line))
+
+
+def tensor_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_cpu_baseline(args, table, s2, x, ti, tv):
+    """The C oracle's restatement of the expert loop (qwen_engine.py:838-852) on this host's cores for
+    the first `cpu_tokens` tokens of step 0 (every expert those tokens route to)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import numpy as np
+    import oracle
+    cores = oracle.threads(os.cpu_count())
+    n = min(args.cpu_tokens, x.shape[0])
+    ti_n = ti[:n].cpu().numpy().astype(np.int32)
+    used = sorted(set(ti_n.ravel().tolist()))
+    remap = {e: i for i, e in enumerate(used)}
+    blocks = table.slots[used].cpu().numpy()
+    ti_local = np.vectorize(remap.get)(ti_n).astype(np.int32)
+    s2_local = s2[used].cpu().numpy()
+    xf = x[:n].float().cpu().numpy()
+    tvf = tv[:n].float().cpu().numpy()
+    t0 = time.perf_counter()
+    oracle.moe_prefill(xf, ti_local, tvf, blocks, 0, s2_local)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} tokens of step 0 ({len(used)} experts: block dequant + fp32 GEMMs + index_add), "
+                      f"{dt:.1f} s"}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.workload == "prefill":
+        return run_prefill(args, rank, world)
 
     import torch
     import qmoe

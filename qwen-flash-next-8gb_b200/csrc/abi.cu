@@ -200,3 +200,70 @@ int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, u
 
 }  // namespace qfn
 
+namespace {
+struct TmapNdEntry {
+  const void* base;
+  int dtype, device, rank;
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  CUtensorMap map;
+};
+constexpr int kTmapNdSlots = 32;
+TmapNdEntry g_tmapsnd[kTmapNdSlots];
+int g_tmapnd_count = 0, g_tmapnd_next = 0;
+}  // namespace
+
+namespace qfn {
+
+int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out) {
+  if (rank < 1 || rank > 5) return set_error(QFN_ERR_INVALID_ARG, "tensor map rank %d", rank);
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  for (int i = 0; i < g_tmapnd_count; ++i) {
+    const TmapNdEntry& t = g_tmapsnd[i];
+    if (t.base != base || t.dtype != static_cast<int>(dtype) || t.device != device || t.rank != rank) continue;
+    bool same = true;
+    for (int d = 0; d < rank; ++d) same = same && t.dims[d] == dims[d] && t.box[d] == box[d];
+    for (int d = 0; d + 1 < rank; ++d) same = same && t.strides[d] == strides[d];
+    if (same) {
+      *out = t.map;
+      return QFN_OK;
+    }
+  }
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || !fn) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  CUtensorMap m;
+  cuuint64_t d64[5], s64[4];
+  cuuint32_t b32[5], es[5];
+  for (int d = 0; d < rank; ++d) {
+    d64[d] = dims[d];
+    b32[d] = box[d];
+    es[d] = 1;
+  }
+  for (int d = 0; d + 1 < rank; ++d) s64[d] = strides[d];
+  CUresult r = g_encode(&m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d64, s64, b32, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled (%d-D) failed (%d)", rank, static_cast<int>(r));
+  TmapNdEntry& t = g_tmapsnd[g_tmapnd_count < kTmapNdSlots ? g_tmapnd_count++ : (g_tmapnd_next++ % kTmapNdSlots)];
+  t.base = base;
+  t.dtype = static_cast<int>(dtype);
+  t.device = device;
+  t.rank = rank;
+  for (int d = 0; d < rank; ++d) {
+    t.dims[d] = dims[d];
+    t.box[d] = box[d];
+  }
+  for (int d = 0; d + 1 < rank; ++d) t.strides[d] = strides[d];
+  t.map = m;
+  *out = m;
+  return QFN_OK;
+}
+
+}  // namespace qfn
+

@@ -379,3 +379,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
 }
 }  // namespace qfn
 
+namespace qfn {
+// 4-D tiled TMA load (box of the tensor map) into shared memory.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, int y, int z, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+}  // namespace qfn
+
+namespace qfn {
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+}  // namespace qfn
+

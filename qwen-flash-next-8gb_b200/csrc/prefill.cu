@@ -12,23 +12,25 @@
 //     tiles of up to 128 pairs of one expert.
 //  2. pf_gather_x: the x row of every pair in pair order, as f16 scaled by a
 //     power of two per token (max |x| in [2^14, 2^15)): exact for bf16 x.
-//  3. pf_gemm<GATEUP>: per (tile, 64 features): D[128 rows][pairs] = A x B^T
-//     on tcgen05 (kind::f16, fp32 accumulators in TMEM).  A = 64 gate rows +
-//     64 up rows of the expert, dequantised from NVFP4 to f16 in shared memory
-//     (e2m1 x E4M3 is exact in f16), B = the tile's x rows (TMA, 128-byte
-//     swizzle).  Epilogue: h = silu(ws2_g g) * (ws2_u u) in fp32.
+//  3. pf_gemm<GATEUP>: per (tile, 128 features): D[128 rows][pairs] = A x B^T
+//     twice (gate rows, up rows) on tcgen05 (kind::f16, fp32 accumulators in
+//     TMEM).  A = the expert's rows dequantised from NVFP4 to f16 in shared
+//     memory (e2m1 x E4M3 is exact in f16), B = the tile's x rows (TMA,
+//     128-byte swizzle).  Epilogue: h = silu(ws2_g g) * (ws2_u u) in fp32.
 //  4. pf_hpack: h rows -> f16 hi + lo (h * 2^e = hi + lo, one e per pair).
 //  5. out = 0.
-//  6. pf_gemm<DOWN>: per (tile, 128 output rows): A = down rows, B = h hi
-//     and h lo (two MMAs into one accumulator: ~22-bit h), epilogue adds
+//  6. pf_gemm<DOWN>: per (tile, 128 output rows): A = down rows, B = the
+//     tile's h hi rows followed by its h lo rows (one MMA computes both;
+//     the epilogue sums the two column blocks: ~22-bit h), and adds
 //     coef * ws2_d * D into out with fp32 atomics (as index_add_ on CUDA).
 //
 // pf_gemm is persistent (one CTA per SM) and warp-specialised: warp 0 issues
-// TMA loads (activation tiles, raw e2m1 rows, scale rows) into a ring of
-// stages; warps 4-7 dequantise the raw rows of each stage into the f16 A
-// tile; one thread of warp 1 issues the MMAs; warps 8-11 drain the TMEM
-// accumulators (two, so the epilogue of one job overlaps the next job's
-// MMAs).  Every wait is bounded; a wait that runs out sets a status bit.
+// TMA loads (activation tiles, raw e2m1 rows) into a ring of stages; warps
+// 4-11 dequantise the raw rows of each stage into two f16 A tiles (their
+// scale rows stream from global memory ahead of use); one thread of warp 1
+// issues the MMAs; warps 12-15 drain the TMEM accumulators (two sets, so the
+// epilogue of one job overlaps the next job's MMAs).  Every wait is bounded;
+// a wait that runs out sets a status bit.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -37,7 +39,7 @@
 namespace qfn {
 
 constexpr int kPfRows = 128;           // pairs per tile (MMA N <= 128) and A rows (MMA M)
-constexpr int kPfThreads = 384;
+constexpr int kPfThreads = 512;
 constexpr int kPfMaxExperts = 1024;
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
@@ -210,34 +212,56 @@ __global__ void __launch_bounds__(160) pf_hpack_kernel(const float* __restrict__
 
 enum { kGateUp = 0, kDown = 1 };
 
+// A job is (tile of <= 128 pairs, 256 weight rows): gate/up jobs take 128
+// features (their 128 gate rows and 128 up rows: two M = 128 accumulators
+// that hold g and u of the same feature in the same TMEM lane); down jobs
+// take 256 output rows (two accumulators of 128 rows).
 template <int MODE>
 struct PfCfg;
 template <>
 struct PfCfg<kGateUp> {
-  static constexpr int kStages = 4;
-  static constexpr int kKBlocks = kHid / 64;   // 40 K-blocks of 64
-  static constexpr int kSub = kInter / 64;     // 10 jobs (64 features each) per tile
-  static constexpr int kBBytes = 16384;        // x tile: 128 rows x 64 f16
-  static constexpr int kScBytes = 2 * 64 * 160;  // gate + up scale rows of 64 features
+  static constexpr int kBStages = 5;            // activation tiles (freed by the MMAs)
+  static constexpr int kRStages = 4;            // raw weight rows (freed by the dequantisers)
+  static constexpr int kAStages = 3;            // dequantised A: gate tile + up tile (2 x 16 KB)
+  static constexpr int kKBlocks = kHid / 64;    // 40 K-blocks of 64
+  static constexpr int kSub = kInter / 128;     // 5 jobs (128 features) per tile
+  static constexpr int kBMax = 16384;           // x tile: <= 128 rows x 64 f16
+  static constexpr int kRaw = 8192;             // 256 raw rows x 32 B
+  static constexpr int kABytes = 32768;
+  static constexpr int kScGroups = 10;          // scale loads per job (16 B = 4 K-blocks each)
+  static constexpr int kScPerGroup = 4;
 };
 template <>
 struct PfCfg<kDown> {
-  static constexpr int kStages = 3;
+  static constexpr int kBStages = 4;
+  static constexpr int kRStages = 4;
+  static constexpr int kAStages = 4;            // dequantised A: one 16 KB tile
   static constexpr int kKBlocks = kInter / 64;  // 10
-  static constexpr int kSub = kHid / 128;       // 20 jobs (128 output rows each) per tile
-  static constexpr int kBBytes = 32768;         // h hi and h lo tiles
-  static constexpr int kScBytes = 128 * 40;     // scale rows of 128 down rows
+  static constexpr int kSub = kHid / 128;       // 20 jobs (128 output rows) per tile
+  static constexpr int kBMax = 32768;           // h hi rows, then h lo rows (one MMA: N = 2 x box rows)
+  static constexpr int kRaw = 4096;             // 128 raw rows x 32 B
+  static constexpr int kABytes = 16384;
+  static constexpr int kScGroups = 5;           // 8 B = 2 K-blocks each
+  static constexpr int kScPerGroup = 2;
 };
 
 template <int MODE>
 struct PfSmem {
+  using C = PfCfg<MODE>;
   static constexpr int kB = 0;
-  static constexpr int kA = kB + PfCfg<MODE>::kStages * PfCfg<MODE>::kBBytes;
-  static constexpr int kRaw = kA + PfCfg<MODE>::kStages * 16384;
-  static constexpr int kSc = kRaw + PfCfg<MODE>::kStages * 4096;
-  static constexpr int kBar = kSc + 2 * PfCfg<MODE>::kScBytes;
-  static constexpr int kCols = kBar + 256;     // per-column epilogue data: 2 x 3 x 128 words
+  static constexpr int kA = kB + C::kBStages * C::kBMax;
+  static constexpr int kRaw = kA + C::kAStages * C::kABytes;
+  static constexpr int kBar = kRaw + C::kRStages * C::kRaw;
+  static constexpr int kCols = kBar + 512;     // per-column epilogue data: 2 x 3 x 128 words
   static constexpr int kTotal = kCols + 2 * 3 * 128 * 4 + 1024;  // + alignment slack
+};
+
+// Activation tensor maps with boxes of 16, 32, 64 and 128 rows (a job loads
+// the smallest box that holds its tile), and the raw weight rows.
+struct PfMaps {
+  CUtensorMap b[4];
+  CUtensorMap b_lo[4];  // down: h lo (gate/up: unused)
+  CUtensorMap w;
 };
 
 struct PfArgs {
@@ -247,11 +271,12 @@ struct PfArgs {
   const int* tile_n;
   const int* pair_tok;
   const float* pair_w;
-  const int* pair_ex;  // x exponent (GATEUP) or h exponent (DOWN) per pair
-  int64_t base;        // table block of expert 0
-  const float* s2l;    // [E][3]
-  float* h32;          // GATEUP output [P][640]
-  float* out;          // DOWN output [T][2560] (accumulated)
+  const int* pair_ex;    // x exponent (GATEUP) or h exponent (DOWN) per pair
+  const uint8_t* table;  // expert blocks (the scale rows are read from here)
+  int64_t base;          // table block of expert 0
+  const float* s2l;      // [E][3]
+  float* h32;            // GATEUP output [P][640]
+  float* out;            // DOWN output [T][2560] (accumulated)
 };
 
 // Bounded wait.  After the first wait of a CTA runs out (`abort`, a word in
@@ -267,21 +292,26 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
 }
 
 template <int MODE>
+__device__ __forceinline__ uint32_t pf_scale_word(const uint4& g, int kb) {
+  const int c = kb & 3;
+  return c == 0 ? g.x : (c == 1 ? g.y : (c == 2 ? g.z : g.w));
+}
+
+template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
-    pf_gemm_kernel(const __grid_constant__ CUtensorMap map_b0, const __grid_constant__ CUtensorMap map_b1,
-                   const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
-                   const PfArgs args) {
+    pf_gemm_kernel(const __grid_constant__ PfMaps maps, const PfArgs args) {
   using C = PfCfg<MODE>;
   using L = PfSmem<MODE>;
-  constexpr int S = C::kStages, KB = C::kKBlocks;
+  constexpr int BS = C::kBStages, RS = C::kRStages, AS = C::kAStages, KB = C::kKBlocks;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* a_ready = full + S;
-  uint64_t* empty = a_ready + S;
-  uint64_t* sc_full = empty + S;
-  uint64_t* sc_empty = sc_full + 2;
-  uint64_t* tm_full = sc_empty + 2;
+  uint64_t* b_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* b_empty = b_full + BS;   // MMA
+  uint64_t* r_full = b_empty + BS;
+  uint64_t* r_empty = r_full + RS;   // 8 dequant warps
+  uint64_t* a_full = r_empty + RS;   // 8 dequant warps
+  uint64_t* a_empty = a_full + AS;   // MMA
+  uint64_t* tm_full = a_empty + AS;
   uint64_t* tm_empty = tm_full + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(tm_empty + 2);
   volatile uint32_t* abort = tslot + 1;
@@ -290,25 +320,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort = 0u;
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&a_ready[s], 4);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < BS; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 8);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&a_full[s], 8);
+      mbar_init(&a_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sc_full[b], 1);
-      mbar_init(&sc_empty[b], 4);
       mbar_init(&tm_full[b], 1);
       mbar_init(&tm_empty[b], 4);
     }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tslot, 256);
+  if (warp == 1) tmem_alloc(tslot, 512);
   if (threadIdx.x == 32) {
-    prefetch_tensormap(&map_b0);
-    prefetch_tensormap(&map_w);
-    prefetch_tensormap(&map_s);
-    if (MODE == kDown) prefetch_tensormap(&map_b1);
+    for (int h = 0; h < 4; ++h) {
+      prefetch_tensormap(&maps.b[h]);
+      if (MODE == kDown) prefetch_tensormap(&maps.b_lo[h]);
+    }
+    prefetch_tensormap(&maps.w);
   }
   tc_fence_before();
   __syncthreads();
@@ -317,128 +353,172 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int n_jobs = args.hdr[0] * C::kSub;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- producer
-    int it = 0, jj = 0;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
-      const int t = u / C::kSub, sub = u % C::kSub;
-      const int e = args.tile_e[t], p0 = args.tile_p0[t];
-      const int64_t blk = args.base + e;
-      const int sb = jj & 1;
-      pf_wait(&sc_empty[sb], ((jj >> 1) & 1) ^ 1, abort);
-      uint8_t* sc = smem + L::kSc + sb * C::kScBytes;
-      mbar_arrive_expect_tx(&sc_full[sb], C::kScBytes);
+    // ---------------- producer: per K-block the tile's activation rows (two
+    // tiles for down: h hi, h lo) in the smallest box that holds them, and
+    // one box of the job's raw weight rows.  At the start of each job the
+    // next job's raw rows are prefetched into L2, so the per-K-block loads
+    // of raw rows hit L2.
+    auto prefetch_job = [&](int ux) {
+      if (ux >= n_jobs) return;
+      const int tx = ux / C::kSub, subx = ux % C::kSub;
+      const uint8_t* blkp = args.table + (args.base + args.tile_e[tx]) * kBlock;
       if (MODE == kGateUp) {
-        const int f0 = 64 * sub;
-        tma_load_2d(sc, &map_s, 0, static_cast<int>(blk * 17280 + 15360 + f0), &sc_full[sb]);
-        tma_load_2d(sc + 64 * 160, &map_s, 0, static_cast<int>(blk * 17280 + 16000 + f0), &sc_full[sb]);
+        bulk_prefetch_l2(blkp + kOGW + 128 * subx * (kHid / 2), 128 * (kHid / 2));
+        bulk_prefetch_l2(blkp + kOUW + 128 * subx * (kHid / 2), 128 * (kHid / 2));
       } else {
-        const int r0 = 128 * sub;
-        tma_load_2d(sc, &map_s, 0, static_cast<int>(blk * 34560 + 33280 + r0 / 2), &sc_full[sb]);
+        bulk_prefetch_l2(blkp + kODW + 128 * subx * (kInter / 2), 128 * (kInter / 2));
       }
+    };
+    prefetch_job(blockIdx.x);
+    int it = 0;
+    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
+      prefetch_job(u + gridDim.x);
+      const int t = u / C::kSub, sub = u % C::kSub;
+      const int p0 = args.tile_p0[t], n = args.tile_n[t];
+      const int hb = n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3));
+      const uint32_t bbytes = (16u << hb) * 128u;
+      const int blk = static_cast<int>(args.base + args.tile_e[t]);
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        pf_wait(&empty[s], ((it / S) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&full[s], C::kBBytes + 4096);
-        uint8_t* bt = smem + L::kB + s * C::kBBytes;
-        uint8_t* raw = smem + L::kRaw + s * 4096;
-        tma_load_2d(bt, &map_b0, 64 * kb, p0, &full[s]);
-        if (MODE == kGateUp) {
-          const int f0 = 64 * sub;
-          tma_load_2d(raw, &map_w, 32 * kb, static_cast<int>(blk * 2160 + f0), &full[s]);
-          tma_load_2d(raw + 2048, &map_w, 32 * kb, static_cast<int>(blk * 2160 + 640 + f0), &full[s]);
-        } else {
-          tma_load_2d(bt + 16384, &map_b1, 64 * kb, p0, &full[s]);
-          tma_load_2d(raw, &map_w, 32 * kb, static_cast<int>(blk * 8640 + 5120 + 128 * sub), &full[s]);
-        }
+        const int sb = it % BS, sr = it % RS;
+        pf_wait(&b_empty[sb], ((it / BS) & 1) ^ 1, abort);
+        mbar_arrive_expect_tx(&b_full[sb], (MODE == kDown ? 2 : 1) * bbytes);
+        uint8_t* bt = smem + L::kB + sb * C::kBMax;
+        tma_load_2d(bt, &maps.b[hb], 64 * kb, p0, &b_full[sb]);
+        if (MODE == kDown) tma_load_2d(bt + bbytes, &maps.b_lo[hb], 64 * kb, p0, &b_full[sb]);  // lo after hi
+        pf_wait(&r_empty[sr], ((it / RS) & 1) ^ 1, abort);
+        mbar_arrive_expect_tx(&r_full[sr], C::kRaw);
+        uint8_t* raw = smem + L::kRaw + sr * C::kRaw;
+        if (MODE == kGateUp)
+          tma_load_4d(raw, &maps.w, 32 * kb, 128 * sub, 0, blk, &r_full[sr]);  // [gate|up][128][32 B]
+        else
+          tma_load_2d(raw, &maps.w, 32 * kb, blk * 8640 + 5120 + 128 * sub, &r_full[sr]);  // [128][32 B]
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     int it = 0, jj = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
-      const int t = u / C::kSub;
-      const int n = args.tile_n[t];
-      const int N = n <= 16 ? 16 : (n + 15) & ~15;
+      const int n = args.tile_n[u / C::kSub];
+      const int rows = 16 << (n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)));  // activation box rows
+      // gate/up: the tile's pairs (rounded up to 16); down: h hi rows then h lo rows of the box
+      const int N = MODE == kDown ? 2 * rows : (n <= 16 ? 16 : (n + 15) & ~15);
       const uint32_t idesc = idesc_f16(128, N);
       const int ab = jj & 1;
-      const uint32_t d = tmem + 128 * ab;
+      const uint32_t d0 = tmem + 256 * ab, d1 = d0 + 128;
       pf_wait(&tm_empty[ab], ((jj >> 1) & 1) ^ 1, abort);
       tc_fence_after();
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        pf_wait(&a_ready[s], (it / S) & 1, abort);
-        pf_wait(&full[s], (it / S) & 1, abort);
+        const int sb = it % BS, sa = it % AS;
+        pf_wait(&a_full[sa], (it / AS) & 1, abort);
+        pf_wait(&b_full[sb], (it / BS) & 1, abort);
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + L::kA + s * 16384);
-        const uint32_t b0 = smem_u32(smem + L::kB + s * C::kBBytes);
+        const uint32_t a0 = smem_u32(smem + L::kA + sa * C::kABytes), a1 = a0 + 16384;
+        const uint32_t b0 = smem_u32(smem + L::kB + sb * C::kBMax);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          mma_f16(d, umma_desc_sw128(a0 + 32 * k, 1024), umma_desc_sw128(b0 + 32 * k, 1024), idesc, kb > 0 || k > 0);
-          if (MODE == kDown)
-            mma_f16(d, umma_desc_sw128(a0 + 32 * k, 1024), umma_desc_sw128(b0 + 16384 + 32 * k, 1024), idesc, true);
+          const bool acc = kb > 0 || k > 0;
+          const uint64_t bd = umma_desc_sw128(b0 + 32 * k, 1024);
+          mma_f16(d0, umma_desc_sw128(a0 + 32 * k, 1024), bd, idesc, acc);
+          if (MODE == kGateUp) mma_f16(d1, umma_desc_sw128(a1 + 32 * k, 1024), bd, idesc, acc);
         }
-        mma_commit(&empty[s]);
+        mma_commit(&b_empty[sb]);
+        mma_commit(&a_empty[sa]);
       }
       mma_commit(&tm_full[ab]);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---------------- dequantisers: thread r builds A row r of every stage
-    const int r = threadIdx.x - 128;
-    int src_raw, src_sc;  // byte offsets of this row in the raw stage / scale buffer
-    if (MODE == kGateUp) {
-      const int q = r >> 5, i = r & 31;
-      const int f = 16 * q + (i & 15);     // feature within the job's 64
-      src_raw = (i < 16 ? 0 : 2048) + f * 32;
-      src_sc = (i < 16 ? 0 : 64 * 160) + f * 160;
-    } else {
-      src_raw = r * 32;
-      src_sc = r * 40;
-    }
-    const uint32_t a_row = (r >> 3) * 1024 + (r & 7) * 128;
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------- dequantisers.  Gate/up: thread d builds row d % 128 of
+    // A tile d / 128 (the gate rows, then the up rows of the job's 128
+    // features), 64 k per K-block.  Down: threads 2r and 2r + 1 build output
+    // row r of the job's 128, 32 k each.
+    const int d = threadIdx.x - 128;
+    const int i = MODE == kGateUp ? d >> 7 : 0;
+    const int r = MODE == kGateUp ? (d & 127) : (d >> 1);
+    const int hf = MODE == kGateUp ? 0 : (d & 1);      // down: which half of the K-block
+    const uint32_t a_row = i * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+    const int raw_off = MODE == kGateUp ? d * 32 : r * 32 + 16 * hf;
+    // Scale rows stream straight from global memory, three loads ahead of
+    // use, continuing across job boundaries.
+    auto sc_ptr = [&](int jjx, int g) -> const uint8_t* {
+      const int ux = blockIdx.x + jjx * gridDim.x;
+      if (ux >= n_jobs) return nullptr;
+      const int tx = ux / C::kSub, subx = ux % C::kSub;
+      const uint8_t* blkp = args.table + (args.base + args.tile_e[tx]) * kBlock;
+      if (MODE == kGateUp) return blkp + (i ? kOUS : kOGS) + (128 * subx + r) * (kHid / 16) + 16 * g;
+      return blkp + kODS + (128 * subx + r) * (kInter / 16) + 8 * g;
+    };
+    auto sc_load = [&](int lin) -> uint4 {
+      const uint8_t* p = sc_ptr(lin / C::kScGroups, lin % C::kScGroups);
+      if (!p) return make_uint4(0, 0, 0, 0);
+      if (MODE == kGateUp) return ldg_stream_v4(p);
+      const uint2 v = ldg_stream_v2(p);
+      return make_uint4(v.x, v.y, 0, 0);
+    };
+    uint4 q0 = sc_load(0), q1 = sc_load(1), q2 = sc_load(2), cur = q0;
     int it = 0, jj = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
-      const int sb = jj & 1;
-      pf_wait(&sc_full[sb], (jj >> 1) & 1, abort);
-      const uint8_t* sc = smem + L::kSc + sb * C::kScBytes + src_sc;
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % S;
-        pf_wait(&full[s], (it / S) & 1, abort);
-        const uint8_t* raw = smem + L::kRaw + s * 4096 + src_raw;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(raw);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(raw + 16);
-        const uint32_t sw = *reinterpret_cast<const uint32_t*>(sc + 4 * kb);
+        if (kb % C::kScPerGroup == 0) {
+          const int lin = jj * C::kScGroups + kb / C::kScPerGroup;
+          cur = q0;
+          q0 = q1;
+          q1 = q2;
+          q2 = sc_load(lin + 3);
+        }
+        const uint32_t sw = MODE == kGateUp ? pf_scale_word<MODE>(cur, kb) : ((kb & 1) ? cur.y : cur.x);
+        const int sr = it % RS, sa = it % AS;
+        pf_wait(&r_full[sr], (it / RS) & 1, abort);
+        pf_wait(&a_empty[sa], ((it / AS) & 1) ^ 1, abort);
+        const uint8_t* raw = smem + L::kRaw + sr * C::kRaw + raw_off;
+        uint8_t* a = smem + L::kA + sa * C::kABytes + a_row;
         uint32_t sa0, sa1, sa2, sa3;
         e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
         e4m3x2_to_bcast(sw >> 16, sa2, sa3);
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint8_t* a = smem + L::kA + s * 16384 + a_row;
+        if (MODE == kGateUp) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + 16);
+          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint32_t h[4];
-          e2m1x8_to_f16x2(words[j], h);
-          const uint32_t sc2 = j < 2 ? sa0 : (j < 4 ? sa1 : (j < 6 ? sa2 : sa3));
-          const uint4 o = make_uint4(hmul2_u32(h[0], sc2), hmul2_u32(h[1], sc2), hmul2_u32(h[2], sc2),
-                                     hmul2_u32(h[3], sc2));
-          *reinterpret_cast<uint4*>(a + ((j ^ (r & 7)) << 4)) = o;
+          for (int j = 0; j < 8; ++j) {
+            uint32_t h[4];
+            e2m1x8_to_f16x2(words[j], h);
+            const uint32_t sc2 = j < 2 ? sa0 : (j < 4 ? sa1 : (j < 6 ? sa2 : sa3));
+            const uint4 o = make_uint4(hmul2_u32(h[0], sc2), hmul2_u32(h[1], sc2), hmul2_u32(h[2], sc2),
+                                       hmul2_u32(h[3], sc2));
+            *reinterpret_cast<uint4*>(a + ((j ^ (r & 7)) << 4)) = o;
+          }
+        } else {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw);
+          const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t s0 = hf ? sa2 : sa0, s1 = hf ? sa3 : sa1;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t h[4];
+            e2m1x8_to_f16x2(words[j], h);
+            const uint32_t sc2 = j < 2 ? s0 : s1;
+            const uint4 o = make_uint4(hmul2_u32(h[0], sc2), hmul2_u32(h[1], sc2), hmul2_u32(h[2], sc2),
+                                       hmul2_u32(h[3], sc2));
+            *reinterpret_cast<uint4*>(a + (((4 * hf + j) ^ (r & 7)) << 4)) = o;
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_ready[s]);
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          mbar_arrive(&r_empty[sr]);
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sc_empty[sb]);
     }
-  } else if (warp >= 8) {
-    // ---------------- epilogue: warp 8 + q reads TMEM lanes 32q .. 32q + 31
-    const int q = warp - 8;
-    const int et = threadIdx.x - 256;  // 0..127
+  } else if (warp >= 12) {
+    // ---------------- epilogue: warp 12 + q reads TMEM lanes 32q .. 32q + 31
+    const int q = warp - 12;
+    const int et = threadIdx.x - 384;  // 0..127
     int jj = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       const int t = u / C::kSub, sub = u % C::kSub;
       const int e = args.tile_e[t], p0 = args.tile_p0[t], n = args.tile_n[t];
       const int ab = jj & 1;
       int* ccol = cols + ab * 3 * 128;
-      // per-column data of this job (all four epilogue warps, then a named barrier)
       if (et < n) {
         ccol[et] = args.pair_tok[p0 + et];
         ccol[128 + et] = __float_as_int(args.pair_w[p0 + et]);
@@ -447,41 +527,40 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
       pf_wait(&tm_full[ab], (jj >> 1) & 1, abort);
       tc_fence_after();
-      const uint32_t taddr = tmem + 128 * ab + (static_cast<uint32_t>(32 * q) << 16);
+      const uint32_t t0 = tmem + 256 * ab + (static_cast<uint32_t>(32 * q) << 16), t1 = t0 + 128;
       if (MODE == kGateUp) {
         const float ws_g = args.s2l[3 * e + 0], ws_u = args.s2l[3 * e + 1];
-        const int feat = 64 * sub + 16 * q + (lane & 15);
+        float* hrow = args.h32 + 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld_x32(taddr + c0, v);
+          uint32_t vg[32], vu[32];
+          tmem_ld_x32(t0 + c0, vg);
+          tmem_ld_x32(t1 + c0, vu);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const float mine = __uint_as_float(v[c]);
-            const float up = __shfl_down_sync(0xffffffffu, mine, 16);
             const int col = c0 + c;
-            if (lane < 16 && col < n) {
+            if (col < n) {
               const int ex = ccol[256 + col];
-              const float g = pow2_mul(mine, -ex) * ws_g;
-              const float uu = pow2_mul(up, -ex) * ws_u;
-              args.h32[static_cast<int64_t>(p0 + col) * kInter + feat] = g / (1.0f + expf(-g)) * uu;
+              const float g = pow2_mul(__uint_as_float(vg[c]), -ex) * ws_g;
+              const float uu = pow2_mul(__uint_as_float(vu[c]), -ex) * ws_u;
+              hrow[static_cast<int64_t>(p0 + col) * kInter] = g / (1.0f + expf(-g)) * uu;
             }
           }
         }
       } else {
         const float ws_d = args.s2l[3 * e + 2];
+        const int rows = 16 << (n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)));
         const int row = 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld_x32(taddr + c0, v);
+          uint32_t vh[32], vl[32];
+          tmem_ld_x32(t0 + c0, vh);
+          tmem_ld_x32(t0 + rows + c0, vl);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const int col = c0 + c;
             if (col < n) {
-              const int tok = ccol[col];
-              const float w = __int_as_float(ccol[128 + col]);
-              const int eh = ccol[256 + col];
-              const float val = pow2_mul(__uint_as_float(v[c]), -eh) * ws_d * w;
-              atomicAdd(args.out + static_cast<int64_t>(tok) * kHid + row, val);
+              const float f = pow2_mul(__int_as_float(ccol[128 + col]) * ws_d, -ccol[256 + col]);
+              atomicAdd(args.out + static_cast<int64_t>(ccol[col]) * kHid + row,
+                        (__uint_as_float(vh[c]) + __uint_as_float(vl[c])) * f);
             }
           }
         }
@@ -493,7 +572,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -528,8 +607,7 @@ static PfWs pf_ws_map(int64_t T, int topk, int E) {
 }
 
 template <int MODE>
-static int pf_launch_gemm(const CUtensorMap& b0, const CUtensorMap& b1, const CUtensorMap& w, const CUtensorMap& s,
-                          const PfArgs& a, const DeviceInfo* dev, cudaStream_t st) {
+static int pf_launch_gemm(const PfMaps& maps, const PfArgs& a, const DeviceInfo* dev, cudaStream_t st) {
   constexpr int smem = PfSmem<MODE>::kTotal;
   static bool attr_set[64] = {};
   if (!attr_set[dev->device]) {
@@ -537,7 +615,7 @@ static int pf_launch_gemm(const CUtensorMap& b0, const CUtensorMap& b1, const CU
     if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "prefill gemm smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev->device] = true;
   }
-  pf_gemm_kernel<MODE><<<dev->sm_count, kPfThreads, smem, st>>>(b0, b1, w, s, a);
+  pf_gemm_kernel<MODE><<<dev->sm_count, kPfThreads, smem, st>>>(maps, a);
   return check_launch(MODE == kGateUp ? "pf_gemm<gate/up>" : "pf_gemm<down>");
 }
 
@@ -614,32 +692,34 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   if ((rc = check_launch("pf_gather_x"))) return rc;
 
   // tensor maps
-  CUtensorMap m_x, m_gw, m_gs, m_dw, m_ds, m_hhi, m_hlo;
-  if ((rc = tensor_map_2d(x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kHid, P, kHid * 2, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &m_x)))
-    return rc;
-  if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1280, n_blocks * 2160, 1280, 32, 64,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &m_gw)))
-    return rc;
-  if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 160, n_blocks * 17280, 160, 160, 64,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &m_gs)))
-    return rc;
+  PfMaps gu_maps, dn_maps;
+  for (int hb = 0; hb < 4; ++hb) {
+    const uint32_t rows = 16u << hb;
+    if ((rc = tensor_map_2d(x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kHid, P, kHid * 2, 64, rows,
+                            CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &gu_maps.b[hb])))
+      return rc;
+    gu_maps.b_lo[hb] = gu_maps.b[hb];
+    if ((rc = tensor_map_2d(hhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kInter, P, kInter * 2, 64, rows,
+                            CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &dn_maps.b[hb])))
+      return rc;
+    if ((rc = tensor_map_2d(hlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kInter, P, kInter * 2, 64, rows,
+                            CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &dn_maps.b_lo[hb])))
+      return rc;
+  }
+  {  // gate and up rows of a block: [block][gate|up][640 rows][1280 B]
+    const uint64_t dims[4] = {1280, 640, 2, static_cast<uint64_t>(n_blocks)};
+    const uint64_t strides[3] = {1280, 819200, static_cast<uint64_t>(kBlock)};
+    const uint32_t box[4] = {32, 128, 2, 1};
+    if ((rc = tensor_map_nd(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, dims, strides, box, dev->device, &gu_maps.w)))
+      return rc;
+  }
   if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 320, n_blocks * 8640, 320, 32, 128,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &m_dw)))
-    return rc;
-  if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 80, n_blocks * 34560, 80, 80, 64,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &m_ds)))
-    return rc;
-  if ((rc = tensor_map_2d(hhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kInter, P, kInter * 2, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &m_hhi)))
-    return rc;
-  if ((rc = tensor_map_2d(hlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kInter, P, kInter * 2, 64, 128,
-                          CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &m_hlo)))
+                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &dn_maps.w)))
     return rc;
 
   // 3. gate/up
-  PfArgs a{hdr, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, base, s2l, h32, out};
-  if ((rc = pf_launch_gemm<kGateUp>(m_x, m_x, m_gw, m_gs, a, dev, st))) return rc;
+  PfArgs a{hdr, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, table, base, s2l, h32, out};
+  if ((rc = pf_launch_gemm<kGateUp>(gu_maps, a, dev, st))) return rc;
   // 4. h -> f16 hi/lo
   pf_hpack_kernel<<<static_cast<unsigned>(P), 160, 0, st>>>(h32, hdr, hhi, hlo, pair_eh);
   if ((rc = check_launch("pf_hpack"))) return rc;
@@ -647,7 +727,7 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * kHid * sizeof(float), st);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_moe_prefill: memset: %s", cudaGetErrorString(e));
   a.pair_ex = pair_eh;
-  return pf_launch_gemm<kDown>(m_hhi, m_hlo, m_dw, m_ds, a, dev, st);
+  return pf_launch_gemm<kDown>(dn_maps, a, dev, st);
 }
 
 extern "C" int qfn_prefill_status(unsigned int* status, int clear) {
