@@ -215,12 +215,20 @@ def run_prefill(args, rank, world):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    dist = shard = None
     if world > 1:
-        raise SystemExit("bench.py --workload prefill runs on one GPU (expert-parallel prefill: see --gpus 1)")
-    table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=N_EXPERTS)
-    table.fill_synthetic(seed=args.seed)
+        import datetime
+        import torch.distributed as dist
+        import ep
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        shard = ep.ExpertShard(N_EXPERTS, world, rank)
+    # expert-parallel: this rank holds 512 / world experts of the layer (its shard)
+    e_local = N_EXPERTS // world
+    table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=e_local)
+    table.fill_synthetic(seed=args.seed + rank)
     s2 = table.s2[0].contiguous()
     R = 4
+    args.seed += 1000 * rank              # every rank routes its own tokens (same popularity permutation)
     xs, tis, tvs = prefill_inputs(args, dev, R)
     T = args.tokens
     pairs = T * PF_TOPK
@@ -228,11 +236,18 @@ def run_prefill(args, rank, world):
     layer_bytes = [d * BLOCK + T * HID * 2 + T * HID * 4 for d in distinct]
 
     def step(i):
-        return qmoe.moe_prefill(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0)
+        if shard is None:
+            return qmoe.moe_prefill(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0)
+        return ep.moe_prefill_ep(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0, shard)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
 
     for i in range(max(args.warmup, 3)):
         step(i)
-    torch.cuda.synchronize()
+    barrier()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -244,10 +259,14 @@ def run_prefill(args, rank, world):
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1) / args.steps
-    tok_s = T / (ms * 1e-3)
-    tflops = pairs * PF_FLOP_PER_PAIR / (ms * 1e-3) / 1e12
+    if dist is not None:
+        t_ = torch.tensor([ms], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms = float(t_.item())
+    tok_s = world * T / (ms * 1e-3)
+    tflops = world * pairs * PF_FLOP_PER_PAIR / (ms * 1e-3) / 1e12
     avg_bytes = sum(layer_bytes[i % R] for i in range(args.steps)) / args.steps
-    gbs = avg_bytes / (ms * 1e-3) / 1e9
+    gbs = avg_bytes / (ms * 1e-3) / 1e9       # one rank's expert bytes (for world > 1: its shard's share)
 
     # e2e: host buffers in (x, ti, tv) and the fp32 result out, every step
     h_x = [x.cpu().pin_memory() for x in xs]
@@ -262,19 +281,26 @@ def run_prefill(args, rank, world):
         d_x.copy_(h_x[i % R], non_blocking=True)
         d_ti.copy_(h_ti[i % R], non_blocking=True)
         d_tv.copy_(h_tv[i % R], non_blocking=True)
-        y = qmoe.moe_prefill(d_x, d_ti, d_tv, table.slots, s2, 0)
+        if shard is None:
+            y = qmoe.moe_prefill(d_x, d_ti, d_tv, table.slots, s2, 0)
+        else:
+            y = ep.moe_prefill_ep(d_x, d_ti, d_tv, table.slots, s2, 0, shard)
         h_out.copy_(y, non_blocking=True)
 
     E = min(args.e2e_steps, args.steps)
     for i in range(2):
         e2e_step(i)
-    torch.cuda.synchronize()
+    barrier()
     e0.record(st)
     for i in range(E):
         e2e_step(i)
     e1.record(st)
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / E
+    if dist is not None:
+        t_ = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t_.item())
 
     tc_peak, tc_kind = tensor_peak()
     line = {
@@ -282,13 +308,15 @@ def run_prefill(args, rank, world):
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, "
                                       "fp32 accumulate", "data": "synthetic",
-        "config": {"workload": f"prefill-moe-1L (config 3): {T} tokens, top-{PF_TOPK} of {N_EXPERTS}, Zipf(1.1), "
-                               f"{pairs} pairs, {sum(distinct) / R:.0f} distinct experts per step",
+        "config": {"workload": f"prefill-moe-1L (config 3): {T} tokens per GPU, top-{PF_TOPK} of {N_EXPERTS}, "
+                               f"Zipf(1.1), {pairs} pairs per GPU, {sum(distinct) / R:.0f} distinct experts per step"
+                               f" routed from rank 0's tokens",
                    "tflops": tflops, "hbm_gbs": gbs, "bytes_per_step": avg_bytes,
                    "flop_per_step": pairs * PF_FLOP_PER_PAIR,
                    "l2": "no flush: each step reads >= 1.4 GB of distinct expert blocks (> 126 MB L2)",
-                   "parallelism": "single GPU"},
-        "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                   "parallelism": f"expert-parallel x{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                   else "single GPU"},
+        "e2e": {"value": world * T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
                 "path": "qmoe.moe_prefill (public API) with pinned host inputs and output"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
@@ -298,9 +326,13 @@ def run_prefill(args, rank, world):
         "gpu_launches": args.steps * 6,
         "clocks": clk.summary(),
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = prefill_cpu_baseline(args, table, s2, xs[0], tis[0], tvs[0])
-    print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
 
 
 def tensor_peak():

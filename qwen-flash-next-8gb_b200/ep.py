@@ -1,0 +1,93 @@
+"""Expert-parallel batched prefill over N ranks (one process per GPU).
+
+The layer's n_experts experts are split into N contiguous ranges of
+n_experts / N; rank r holds the blocks of experts [r*E_r, (r+1)*E_r) of every
+layer in its own table (block L * E_r + e_local), and the tokens are split
+across ranks (each rank routes its own tokens).  One MoE layer is then
+
+  1. dispatch: every (token, slot) pair goes to the rank that owns its expert
+     -- counts with one all-to-all, then the pairs' bf16 x rows and their
+     (local expert, routing weight) with two uneven all-to-alls;
+  2. expert compute: the received pairs run through the grouped GEMM
+     (qmoe.moe_prefill) as tokens routed to one local expert each, weight
+     applied;
+  3. combine: the fp32 rows go back with one uneven all-to-all and are added
+     onto their tokens (index_add_, fp32 atomics as in the reference loop,
+     qwen_engine.py:849).
+
+The result on each rank equals the single-GPU qmoe.moe_prefill of its tokens
+(the reference's expert loop, qwen_engine.py:835-852) to fp32 accumulation
+order.  Collectives run on the given process group (NCCL between GPUs; gloo
+works for CPU tensors).  Batched decode uses the same exchange.
+"""
+import torch
+import torch.distributed as dist
+
+import qmoe
+
+
+class ExpertShard:
+    """Contiguous placement of a layer's experts over the ranks of a group."""
+
+    def __init__(self, n_experts, world, rank):
+        if n_experts % world:
+            raise ValueError(f"{n_experts} experts do not split evenly over {world} ranks")
+        self.n_experts, self.world, self.rank = n_experts, world, rank
+        self.per_rank = n_experts // world
+        self.first = rank * self.per_rank
+
+    def owner(self, e):
+        return e // self.per_rank
+
+    def local(self, e):
+        return e - self.owner(e) * self.per_rank
+
+
+def _a2a(out, inp, out_splits, in_splits, group):
+    dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+    return out
+
+
+def moe_prefill_ep(x, ti, tv, table, s2, L, shard, group=None, compute=None):
+    """One expert-parallel MoE layer for this rank's tokens.
+
+    x bf16 [T, 2560] . ti int64/int32 [T, topk] global expert ids of layer L .
+    tv bf16/fp32 [T, topk] . table u8 [n_layers * E_r, BLOCK] this rank's
+    expert blocks . s2 f32 [E_r, 3] ws2 of this rank's experts of layer L .
+    shard: ExpertShard of the group -> fp32 [T, 2560].
+
+    `compute(x_pairs, e_local [R,1], w [R,1], table, s2, L)` defaults to
+    qmoe.moe_prefill (the CUDA kernels); tests substitute a CPU checker to
+    exercise the exchange with gloo.
+    """
+    compute = compute or qmoe.moe_prefill
+    dev = x.device
+    T, K = ti.shape
+    N = shard.world
+    ti_flat = ti.reshape(-1).long()
+    dest = torch.div(ti_flat, shard.per_rank, rounding_mode="floor")
+    order = torch.argsort(dest, stable=True)                       # pairs grouped by owner rank
+    send_counts = torch.bincount(dest, minlength=N)
+    recv_counts = torch.empty_like(send_counts)
+    _a2a(recv_counts, send_counts, None, None, group)
+    send_splits, recv_splits = send_counts.tolist(), recv_counts.tolist()
+    R = sum(recv_splits)
+
+    tok = torch.div(order, K, rounding_mode="floor")
+    x_send = x.index_select(0, tok)
+    meta_send = torch.stack([(ti_flat[order] - dest[order] * shard.per_rank).to(torch.int32),
+                             tv.reshape(-1)[order].float().contiguous().view(torch.int32)], 1).contiguous()
+    x_recv = torch.empty(R, x.shape[1], dtype=x.dtype, device=dev)
+    meta_recv = torch.empty(R, 2, dtype=torch.int32, device=dev)
+    _a2a(x_recv, x_send, recv_splits, send_splits, group)
+    _a2a(meta_recv, meta_send, recv_splits, send_splits, group)
+
+    e_local = meta_recv[:, 0:1].contiguous()
+    w = meta_recv[:, 1:2].contiguous().view(torch.float32)
+    y = compute(x_recv, e_local, w, table, s2, L) if R else torch.empty(0, x.shape[1], dtype=torch.float32,
+                                                                        device=dev)
+    y_back = torch.empty(T * K, x.shape[1], dtype=torch.float32, device=dev)
+    _a2a(y_back, y.contiguous(), send_splits, recv_splits, group)
+    out = torch.zeros(T, x.shape[1], dtype=torch.float32, device=dev)
+    out.index_add_(0, tok, y_back)
+    return out

@@ -1,0 +1,88 @@
+"""Expert-parallel prefill exchange (ep.moe_prefill_ep) with world_size 2 on
+CPU over gloo: dispatch by expert owner, per-rank expert compute, combine.
+
+The per-rank expert compute is the CPU oracle (the checker), injected through
+moe_prefill_ep's `compute` argument; the result on every rank must equal the
+single-process oracle over all tokens with the whole expert table.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+import synthetic
+from conftest import rel_err
+
+E, TOPK, T_PER_RANK, WORLD = 8, 3, 6, 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    blocks = synthetic.make_blocks(E, seed=61)
+    s2 = synthetic.make_s2(E, seed=62, spread=True)
+    T = T_PER_RANK * WORLD
+    x = synthetic.make_x(T * 2560, seed=63, dtype=torch.float32).view(T, 2560).numpy()
+    ti, tv = oracle.route(synthetic.zipf_logits(T, seed=64, n_experts=E), TOPK)
+    return blocks, s2, x, ti, tv
+
+
+def _cpu_compute(x_pairs, e_local, w, table, s2, L):
+    out = oracle.moe_prefill(x_pairs.float().numpy(), e_local.numpy().astype(np.int32), w.numpy(),
+                             table.numpy(), L * s2.shape[0], s2.numpy())
+    return torch.from_numpy(out)
+
+
+def _worker(rank, port, results):
+    import ep
+    os.environ["GLOO_SOCKET_IFNAME"] = "lo"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD)
+    try:
+        blocks, s2, x, ti, tv = _inputs()
+        shard = ep.ExpertShard(E, WORLD, rank)
+        own = slice(shard.first, shard.first + shard.per_rank)
+        toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
+        out = ep.moe_prefill_ep(torch.from_numpy(x[toks]), torch.from_numpy(ti[toks]).long(),
+                                torch.from_numpy(tv[toks]), torch.from_numpy(blocks[own]),
+                                torch.from_numpy(s2[own]), 0, shard, compute=_cpu_compute)
+        results[rank] = out.numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_prefill_matches_single_process():
+    blocks, s2, x, ti, tv = _inputs()
+    # both ranks really exchange: some pairs of each rank's tokens live on the other rank
+    owners = ti // (E // WORLD)
+    assert (owners[:T_PER_RANK] == 1).any() and (owners[T_PER_RANK:] == 0).any()
+    ref = oracle.moe_prefill(x, ti, tv, blocks, 0, s2)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=240)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        out = np.concatenate([results[r] for r in range(WORLD)])
+    assert rel_err(out, ref) <= 1e-5
+
+
+def test_expert_shard_placement():
+    import ep
+    sh = ep.ExpertShard(512, 8, 3)
+    assert sh.per_rank == 64 and sh.first == 192
+    assert sh.owner(191) == 2 and sh.owner(192) == 3 and sh.local(200) == 8
+    with pytest.raises(ValueError):
+        ep.ExpertShard(512, 3, 0)

@@ -1,0 +1,75 @@
+"""Expert-parallel prefill on 2 GPUs over NCCL: each rank holds half of the
+layer's experts and its own tokens; the exchanged result must equal the CPU
+oracle of the whole layer.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synthetic
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+E, TOPK, T_PER_RANK, WORLD = 64, 10, 40, 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    blocks = synthetic.make_blocks(E, seed=71)
+    s2 = synthetic.make_s2(E, seed=72, spread=True)
+    T = T_PER_RANK * WORLD
+    x = synthetic.make_x(T * 2560, seed=73).view(T, 2560)
+    ti, tv = oracle.route(synthetic.zipf_logits(T, seed=74, n_experts=E), TOPK)
+    return blocks, s2, x, ti, tv
+
+
+def _worker(rank, port, results):
+    import datetime
+    import torch.distributed as dist
+    import ep
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        blocks, s2, x, ti, tv = _inputs()
+        shard = ep.ExpertShard(E, WORLD, rank)
+        own = slice(shard.first, shard.first + shard.per_rank)
+        toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
+        out = ep.moe_prefill_ep(x[toks].to(dev), torch.from_numpy(ti[toks]).long().to(dev),
+                                torch.from_numpy(tv[toks]).to(dev).to(torch.bfloat16),
+                                torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0, shard)
+        torch.cuda.synchronize()
+        results[rank] = out.cpu().numpy()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_expert_parallel_prefill_two_gpus_matches_oracle():
+    import torch.multiprocessing as mp
+    blocks, s2, x, ti, tv = _inputs()
+    ref = oracle.moe_prefill(x.float().numpy(), ti, tv, blocks, 0, s2)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        out = np.concatenate([results[r] for r in range(WORLD)])
+    assert rel_err(out, ref) <= 1e-4
