@@ -11,6 +11,14 @@
 
 namespace qfn {
 
+__device__ unsigned int g_gemv_status = 0;
+
+__device__ __forceinline__ float warp_sum_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
 constexpr int kGemvThreads = 256;
 constexpr int kGemvRowsPerWarp = 2;
 constexpr int kGemvRowsPerCta = (kGemvThreads / 32) * kGemvRowsPerWarp;
@@ -107,11 +115,212 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_e4m3_kernel(const uint8_t* 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Stream path (K % 64 == 0, K <= 8192): one CTA of 512 threads per SM owns a
+// contiguous range of 16-row tiles.  Tiles are bulk-copied (TMA, non-tensor:
+// a tile is 16 x K contiguous bytes) into a ring of shared-memory slots, all
+// slots requested at entry, refilled as tiles are consumed.  x is staged once
+// as an f16 hi/lo pair after one power-of-two prescale.  Dot products run on
+// mma.sync.m16n8k16: A = 16 weight rows (E4M3 -> f16 is exact; the row scale
+// is applied to the fp32 result), B = x hi / x lo in columns 0 / 1.  Warp w
+// owns a K-range of 64-element spans of every tile; lane t takes bytes
+// [16t, 16t + 16) of a span's 64 bytes, so one 128-bit load per row feeds
+// four MMAs (the K order inside a span is permuted identically in A and B).
+// Per-warp partial sums meet in shared memory and are added in a fixed order.
+
+constexpr int kGsThreads = 512;
+constexpr int kGsWarps = kGsThreads / 32;
+constexpr int kGsMaxTilesPerCta = 16;
+constexpr int kGsSmemBudget = 225 * 1024;
+
+struct GsLayout {
+  int slots, ring, xs, xraw, red, bar, total;
+};
+
+// Shared memory of the stream path for K and up to `tiles` tiles per CTA:
+// the ring of 16 x K weight slots, x hi/lo (f16), x as loaded (bf16; dead
+// after staging, so it shares its bytes with the per-tile partial sums).
+__host__ __device__ inline GsLayout gs_layout(int K, int tiles) {
+  GsLayout L;
+  const int tile = 16 * K;
+  const int red = tiles * kGsWarps * 16 * 4;
+  const int scratch = red > 2 * K ? red : 2 * K;
+  const int fixed = 4 * K + scratch + 256 + 128;
+  int slots = (kGsSmemBudget - fixed) / tile;
+  slots = slots < 1 ? 1 : (slots > 8 ? 8 : (slots > tiles ? tiles : slots));
+  L.slots = slots;
+  L.ring = 0;
+  L.xs = slots * tile;        // x hi [K] f16, then x lo [K] f16
+  L.xraw = L.xs + 4 * K;      // x as loaded (bf16)
+  L.red = L.xraw;             // [tile][warp][16] fp32 partials (after x is staged)
+  L.bar = L.xraw + scratch;
+  L.total = L.bar + 256 + 128;  // barriers + alignment slack
+  return L;
+}
+
+template <bool kOutF32>
+__global__ void __launch_bounds__(kGsThreads, 1)
+    gemv_stream_kernel(const uint8_t* __restrict__ q, const float* __restrict__ s, const uint16_t* __restrict__ x,
+                       void* __restrict__ y, int64_t N, int K, int max_tiles) {
+  extern __shared__ __align__(128) uint8_t gsm_raw[];
+  uint8_t* sm = gsm_raw + ((128 - (smem_u32(gsm_raw) & 127)) & 127);
+  const GsLayout L = gs_layout(K, max_tiles);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar);
+  uint64_t* empty = full + 9;
+  __shared__ float wmax[kGsWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t n_tiles = (N + 15) / 16;
+  const int64_t t0 = n_tiles * blockIdx.x / gridDim.x, t1 = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int nt = static_cast<int>(t1 - t0);
+  const int S = L.slots;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGsWarps);
+    }
+    mbar_init(&full[8], 1);  // x
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {  // tile i of this CTA into slot i % S
+    const int64_t row0 = (t0 + i) * 16;
+    const int64_t rows = N - row0 < 16 ? N - row0 : 16;
+    const uint32_t bytes = static_cast<uint32_t>(rows * K);
+    mbar_arrive_expect_tx(&full[i % S], bytes);
+    bulk_g2s(sm + L.ring + (i % S) * 16 * K, q + row0 * K, bytes, &full[i % S]);
+  };
+  // Inputs may come from the previous kernel in the stream: wait for it (the
+  // launch and the prologue above overlap its tail).
+  pdl_wait();
+  pdl_launch_dependents();
+  // x first (ordinary loads would queue behind the weight stream), then the tiles.
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&full[8], 2 * K);
+    bulk_g2s(sm + L.xraw, x, 2 * K, &full[8]);
+    for (int i = 0; i < nt && i < S; ++i) issue(i);
+  }
+
+  // x -> f16 hi/lo * 2^ex (thread u owns k = u, u + 512, ...)
+  if (!mbar_wait(&full[8], 0)) atomicOr(&g_gemv_status, kStatusTimeout);
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(sm + L.xraw);
+  constexpr int kMaxPer = 8192 / kGsThreads;
+  float xv[kMaxPer];
+  float mx = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const int k = threadIdx.x + j * kGsThreads;
+    xv[j] = k < K ? bf16_bits_to_f32(xr[k]) : 0.f;
+    mx = fmaxf(mx, fabsf(xv[j]));
+  }
+  mx = warp_sum_max(mx);
+  if (lane == 0) wmax[warp] = mx;
+  __syncthreads();
+  float xm = 0.f;
+  for (int w = 0; w < kGsWarps; ++w) xm = fmaxf(xm, wmax[w]);
+  const int ex = f16_prescale_exp(xm);
+  __half* xh = reinterpret_cast<__half*>(sm + L.xs);
+  __half* xl = xh + K;
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const int k = threadIdx.x + j * kGsThreads;
+    if (k < K) {
+      __half hi, lo;
+      split_f16(ldexpf(xv[j], ex), hi, lo);
+      xh[k] = hi;
+      xl[k] = lo;
+    }
+  }
+  __syncthreads();
+
+  const int spans = K >> 6;
+  const int sp0 = spans * warp / kGsWarps, sp1 = spans * (warp + 1) / kGsWarps;
+  const __half* xsrc = g == 0 ? xh : xl;
+  float* red = reinterpret_cast<float*>(sm + L.red);
+  for (int i = 0; i < nt; ++i) {
+    const int slot = i % S;
+    if (!mbar_wait(&full[slot], (i / S) & 1)) atomicOr(&g_gemv_status, kStatusTimeout);
+    const uint8_t* tile = sm + L.ring + slot * 16 * K;
+    float d4[4][4] = {};  // four independent MMA chains (one per 16-k step of a span)
+    for (int sp = sp0; sp < sp1; ++sp) {
+      const uint4 ra = *reinterpret_cast<const uint4*>(tile + g * K + 64 * sp + 16 * t);
+      const uint4 rb = *reinterpret_cast<const uint4*>(tile + (g + 8) * K + 64 * sp + 16 * t);
+      const uint32_t wa[4] = {ra.x, ra.y, ra.z, ra.w};
+      const uint32_t wb[4] = {rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t alo, ahi, blo, bhi;
+        e4m3x4_to_f16x2(wa[j], alo, ahi);
+        e4m3x4_to_f16x2(wb[j], blo, bhi);
+        const uint32_t a[4] = {alo, blo, ahi, bhi};
+        uint2 bq = make_uint2(0, 0);
+        if (g < 2) bq = *reinterpret_cast<const uint2*>(xsrc + 64 * sp + 16 * t + 4 * j);
+        mma_16816(d4[j], a, bq.x, bq.y);
+      }
+    }
+    if (t == 0) {
+      red[(i * kGsWarps + warp) * 16 + g] =
+          ((d4[0][0] + d4[0][1]) + (d4[1][0] + d4[1][1])) + ((d4[2][0] + d4[2][1]) + (d4[3][0] + d4[3][1]));
+      red[(i * kGsWarps + warp) * 16 + 8 + g] =
+          ((d4[0][2] + d4[0][3]) + (d4[1][2] + d4[1][3])) + ((d4[2][2] + d4[2][3]) + (d4[3][2] + d4[3][3]));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (threadIdx.x == 0 && i + S < nt) {
+      if (!mbar_wait(&empty[slot], (i / S) & 1)) atomicOr(&g_gemv_status, kStatusTimeout);
+      issue(i + S);
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < 16 * nt; r += kGsThreads) {
+    const int i = r >> 4, rr = r & 15;
+    const int64_t row = (t0 + i) * 16 + rr;
+    if (row >= N) continue;
+    float acc = 0.f;
+    for (int w = 0; w < kGsWarps; ++w) acc += red[(i * kGsWarps + w) * 16 + rr];
+    const float v = ldexpf(acc, -ex) * s[row];
+    if (kOutF32) static_cast<float*>(y)[row] = v;
+    else static_cast<__nv_bfloat16*>(y)[row] = __float2bfloat16_rn(v);
+  }
+}
+
 static int launch_gemv(const uint8_t* q, const float* s, const uint16_t* x, void* y, int y_dtype, int64_t N,
                        int64_t K, cudaStream_t st) {
   DeviceInfo* dev;
   int rc = current_device(&dev);
   if (rc) return rc;
+  if (K % 64 == 0 && K <= 8192 && aligned(x, 16)) {
+    const int64_t n_tiles = (N + 15) / 16;
+    int64_t grid = dev->sm_count;
+    if (n_tiles > grid * kGsMaxTilesPerCta) grid = (n_tiles + kGsMaxTilesPerCta - 1) / kGsMaxTilesPerCta;
+    if (grid > n_tiles) grid = n_tiles;
+    const int max_tiles = static_cast<int>((n_tiles + grid - 1) / grid);
+    const GsLayout L = gs_layout(static_cast<int>(K), max_tiles);
+    if (static_cast<size_t>(L.total) + 1024 <= dev->smem_optin && grid <= 65535) {
+      static int attr_set[64][2] = {};  // largest dynamic shared memory enabled so far
+      const int ti = y_dtype == QFN_DTYPE_F32 ? 1 : 0;
+      auto fn = y_dtype == QFN_DTYPE_F32 ? gemv_stream_kernel<true> : gemv_stream_kernel<false>;
+      if (attr_set[dev->device][ti] < L.total) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+        if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "gemv smem attribute: %s", cudaGetErrorString(e));
+        attr_set[dev->device][ti] = L.total;
+      }
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(grid));
+      cfg.blockDim = dim3(kGsThreads);
+      cfg.dynamicSmemBytes = L.total;
+      cfg.stream = st;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaError_t e = cudaLaunchKernelEx(&cfg, fn, q, s, x, y, N, static_cast<int>(K), max_tiles);
+      if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "gemv_stream_kernel launch: %s", cudaGetErrorString(e));
+      return check_launch("gemv_stream_kernel");
+    }
+  }
   const size_t smem = static_cast<size_t>(K) * 4;
   const unsigned grid = static_cast<unsigned>((N + kGemvRowsPerCta - 1) / kGemvRowsPerCta);
   if (y_dtype == QFN_DTYPE_F32) {
