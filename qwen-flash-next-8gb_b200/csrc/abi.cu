@@ -203,7 +203,7 @@ int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, u
 namespace {
 struct TmapNdEntry {
   const void* base;
-  int dtype, device, rank;
+  int dtype, device, rank, swizzle;
   uint64_t dims[5], strides[4];
   uint32_t box[5];
   CUtensorMap map;
@@ -216,12 +216,15 @@ int g_tmapnd_count = 0, g_tmapnd_next = 0;
 namespace qfn {
 
 int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
-                  const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out) {
+                  const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out,
+                  CUtensorMapSwizzle swizzle) {
   if (rank < 1 || rank > 5) return set_error(QFN_ERR_INVALID_ARG, "tensor map rank %d", rank);
   std::lock_guard<std::mutex> lk(g_tmap_mu);
   for (int i = 0; i < g_tmapnd_count; ++i) {
     const TmapNdEntry& t = g_tmapsnd[i];
-    if (t.base != base || t.dtype != static_cast<int>(dtype) || t.device != device || t.rank != rank) continue;
+    if (t.base != base || t.dtype != static_cast<int>(dtype) || t.device != device || t.rank != rank ||
+        t.swizzle != static_cast<int>(swizzle))
+      continue;
     bool same = true;
     for (int d = 0; d < rank; ++d) same = same && t.dims[d] == dims[d] && t.box[d] == box[d];
     for (int d = 0; d + 1 < rank; ++d) same = same && t.strides[d] == strides[d];
@@ -247,7 +250,7 @@ int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const u
   }
   for (int d = 0; d + 1 < rank; ++d) s64[d] = strides[d];
   CUresult r = g_encode(&m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d64, s64, b32, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled (%d-D) failed (%d)", rank, static_cast<int>(r));
   TmapNdEntry& t = g_tmapsnd[g_tmapnd_count < kTmapNdSlots ? g_tmapnd_count++ : (g_tmapnd_next++ % kTmapNdSlots)];
@@ -255,6 +258,7 @@ int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const u
   t.dtype = static_cast<int>(dtype);
   t.device = device;
   t.rank = rank;
+  t.swizzle = static_cast<int>(swizzle);
   for (int d = 0; d < rank; ++d) {
     t.dims[d] = dims[d];
     t.box[d] = box[d];

@@ -55,10 +55,11 @@ int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, u
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle,
                   int device, CUtensorMap* out);
 
-// N-D (rank <= 5) TMA tensor map, no swizzle, cached per (device, arguments).
+// N-D (rank <= 5) TMA tensor map, cached per (device, arguments).
 // dims[0] is the contiguous dimension; strides[i] is the byte stride of
 // dimension i + 1.
 int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
-                  const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out);
+                  const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
 }  // namespace qfn

@@ -212,56 +212,62 @@ __global__ void __launch_bounds__(160) pf_hpack_kernel(const float* __restrict__
 
 enum { kGateUp = 0, kDown = 1 };
 
-// A job is (tile of <= 128 pairs, 256 weight rows): gate/up jobs take 128
+// A job is (tile of <= 128 pairs, 128 weight rows): gate/up jobs take 128
 // features (their 128 gate rows and 128 up rows: two M = 128 accumulators
 // that hold g and u of the same feature in the same TMEM lane); down jobs
-// take 256 output rows (two accumulators of 128 rows).
+// take 128 output rows.
 template <int MODE>
 struct PfCfg;
 template <>
 struct PfCfg<kGateUp> {
-  static constexpr int kBStages = 5;            // activation tiles (freed by the MMAs)
-  static constexpr int kRStages = 4;            // raw weight rows (freed by the dequantisers)
-  static constexpr int kAStages = 3;            // dequantised A: gate tile + up tile (2 x 16 KB)
+  static constexpr int kRStages = 4;            // raw weight rows + scales (freed by the dequantisers)
+  static constexpr int kRawKB = 4;              // K-blocks per raw stage: [gate|up][128 rows][128 B], 128-byte swizzle
   static constexpr int kKBlocks = kHid / 64;    // 40 K-blocks of 64
   static constexpr int kSub = kInter / 128;     // 5 jobs (128 features) per tile
   static constexpr int kBMax = 16384;           // x tile: <= 128 rows x 64 f16
-  static constexpr int kRaw = 8192;             // 256 raw rows x 32 B
-  static constexpr int kABytes = 32768;
-  static constexpr int kScGroups = 10;          // scale loads per job (16 B = 4 K-blocks each)
-  static constexpr int kScPerGroup = 4;
+  static constexpr int kRawBytes = 32768;
+  static constexpr int kRaw = kRawBytes + 4096;  // + [gate|up][128 rows][16 B] scales of the stage's 4 K-blocks
+  static constexpr int kJobScales = 0;
 };
 template <>
 struct PfCfg<kDown> {
-  static constexpr int kBStages = 4;
-  static constexpr int kRStages = 4;
-  static constexpr int kAStages = 4;            // dequantised A: one 16 KB tile
+  static constexpr int kRStages = 6;
+  static constexpr int kRawKB = 2;              // [128 rows][64 B], 64-byte swizzle
   static constexpr int kKBlocks = kInter / 64;  // 10
   static constexpr int kSub = kHid / 128;       // 20 jobs (128 output rows) per tile
   static constexpr int kBMax = 32768;           // h hi rows, then h lo rows (one MMA: N = 2 x box rows)
-  static constexpr int kRaw = 4096;             // 128 raw rows x 32 B
-  static constexpr int kABytes = 16384;
-  static constexpr int kScGroups = 5;           // 8 B = 2 K-blocks each
-  static constexpr int kScPerGroup = 2;
+  static constexpr int kRawBytes = 8192;
+  static constexpr int kRaw = kRawBytes;
+  static constexpr int kJobScales = 128 * (kInter / 16);  // a job's 128 scale rows of 40 B, loaded once per job
 };
+// TMEM: columns [0, 256) hold the accumulators as two halves of 128 columns;
+// a job with <= 64 pairs takes one half (gate/up: g in 64 columns, u in the
+// next 64; down: N = 2 x box rows <= 128), so its epilogue overlaps the next
+// job's MMAs in the other half; a larger job takes both.  Columns
+// [256, 512) are a ring of 4 dequantised A slots of 64 columns (a 128-row x
+// 64-k f16 tile is 32 columns; gate/up jobs use both halves of a slot).
+constexpr int kPfKStages = 4;  // K-block stages: activation tiles in shared memory, A slots in TMEM
+constexpr uint32_t kPfTmemA = 256;
 
 template <int MODE>
 struct PfSmem {
   using C = PfCfg<MODE>;
   static constexpr int kB = 0;
-  static constexpr int kA = kB + C::kBStages * C::kBMax;
-  static constexpr int kRaw = kA + C::kAStages * C::kABytes;
-  static constexpr int kBar = kRaw + C::kRStages * C::kRaw;
+  static constexpr int kRaw = kB + kPfKStages * C::kBMax;
+  static constexpr int kJs = kRaw + C::kRStages * C::kRaw;  // down: two per-job scale buffers
+  static constexpr int kBar = kJs + 2 * C::kJobScales;
   static constexpr int kCols = kBar + 512;     // per-column epilogue data: 2 x 3 x 128 words
   static constexpr int kTotal = kCols + 2 * 3 * 128 * 4 + 1024;  // + alignment slack
 };
 
 // Activation tensor maps with boxes of 16, 32, 64 and 128 rows (a job loads
-// the smallest box that holds its tile), and the raw weight rows.
+// the smallest box that holds its tile), the raw weight rows and the scale
+// rows.
 struct PfMaps {
   CUtensorMap b[4];
   CUtensorMap b_lo[4];  // down: h lo (gate/up: unused)
   CUtensorMap w;
+  CUtensorMap s;
 };
 
 struct PfArgs {
@@ -272,7 +278,7 @@ struct PfArgs {
   const int* pair_tok;
   const float* pair_w;
   const int* pair_ex;    // x exponent (GATEUP) or h exponent (DOWN) per pair
-  const uint8_t* table;  // expert blocks (the scale rows are read from here)
+  const uint8_t* table;  // expert blocks
   int64_t base;          // table block of expert 0
   const float* s2l;      // [E][3]
   float* h32;            // GATEUP output [P][640]
@@ -291,50 +297,58 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
-template <int MODE>
-__device__ __forceinline__ uint32_t pf_scale_word(const uint4& g, int kb) {
-  const int c = kb & 3;
-  return c == 0 ? g.x : (c == 1 ? g.y : (c == 2 ? g.z : g.w));
-}
+// Accumulator halves in use: the MMA issuer and the epilogue walk the same
+// job sequence and keep identical copies of this state.
+struct PfHalves {
+  uint32_t u0 = 0u, u1 = 0u;  // jobs that used half 0 / half 1 so far
+  int next = 0;
+  // the half a job of n pairs takes (2 = both)
+  __device__ __forceinline__ int pick(int n) const { return n > 64 ? 2 : next; }
+  __device__ __forceinline__ void done(int h) {
+    if (h != 1) ++u0;
+    if (h != 0) ++u1;
+    next = h == 0 ? 1 : 0;
+  }
+};
 
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
     pf_gemm_kernel(const __grid_constant__ PfMaps maps, const PfArgs args) {
   using C = PfCfg<MODE>;
   using L = PfSmem<MODE>;
-  constexpr int BS = C::kBStages, RS = C::kRStages, AS = C::kAStages, KB = C::kKBlocks;
+  constexpr int KS = kPfKStages, RS = C::kRStages, KB = C::kKBlocks;
+  constexpr int NI = MODE == kGateUp ? 2 : 1;  // MMA issuers (gate/up: one for the gate rows, one for the up rows)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* b_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* b_empty = b_full + BS;   // MMA
-  uint64_t* r_full = b_empty + BS;
+  // K-block stage s: activation tile s in shared memory + A slot s in TMEM.
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 8 dequant warps
+  uint64_t* k_empty = k_full + KS;   // NI MMA issuers (commit)
+  uint64_t* r_full = k_empty + KS;
   uint64_t* r_empty = r_full + RS;   // 8 dequant warps
-  uint64_t* a_full = r_empty + RS;   // 8 dequant warps
-  uint64_t* a_empty = a_full + AS;   // MMA
-  uint64_t* tm_full = a_empty + AS;
-  uint64_t* tm_empty = tm_full + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tm_empty + 2);
+  uint64_t* tm_full = r_empty + RS;  // [2] accumulator halves: NI MMA issuers -> epilogue
+  uint64_t* tm_empty = tm_full + 2;  // [2] 4 epilogue warps
+  uint64_t* js_full = tm_empty + 2;  // [2] down: per-job scale rows
+  uint64_t* js_empty = js_full + 2;  // [2] 8 dequant warps
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(js_empty + 2);
   volatile uint32_t* abort = tslot + 1;
   int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][3][128]: token, weight bits, exponent
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     *abort = 0u;
-    for (int s = 0; s < BS; ++s) {
-      mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 9);
+      mbar_init(&k_empty[s], NI);
     }
     for (int s = 0; s < RS; ++s) {
       mbar_init(&r_full[s], 1);
       mbar_init(&r_empty[s], 8);
     }
-    for (int s = 0; s < AS; ++s) {
-      mbar_init(&a_full[s], 8);
-      mbar_init(&a_empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tm_full[b], 1);
-      mbar_init(&tm_empty[b], 4);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&tm_full[h], NI);
+      mbar_init(&tm_empty[h], 4);
+      mbar_init(&js_full[h], 1);
+      mbar_init(&js_empty[h], 8);
     }
     fence_mbar_init();
   }
@@ -345,6 +359,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (MODE == kDown) prefetch_tensormap(&maps.b_lo[h]);
     }
     prefetch_tensormap(&maps.w);
+    prefetch_tensormap(&maps.s);
   }
   tc_fence_before();
   __syncthreads();
@@ -353,11 +368,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int n_jobs = args.hdr[0] * C::kSub;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- producer: per K-block the tile's activation rows (two
-    // tiles for down: h hi, h lo) in the smallest box that holds them, and
-    // one box of the job's raw weight rows.  At the start of each job the
-    // next job's raw rows are prefetched into L2, so the per-K-block loads
-    // of raw rows hit L2.
+    // ---------------- activation producer: per K-block the tile's activation
+    // rows (two tiles for down: h hi, h lo) in the smallest box that holds
+    // them, completing on the stage's k_full barrier.
+    int it = 0;
+    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
+      const int t = u / C::kSub;
+      const int p0 = args.tile_p0[t], n = args.tile_n[t];
+      const int hb = n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3));
+      const uint32_t bbytes = (16u << hb) * 128u;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % KS;
+        pf_wait(&k_empty[s], ((it / KS) & 1) ^ 1, abort);
+        mbar_arrive_expect_tx(&k_full[s], (MODE == kDown ? 2 : 1) * bbytes);
+        uint8_t* bt = smem + L::kB + s * C::kBMax;
+        tma_load_2d(bt, &maps.b[hb], 64 * kb, p0, &k_full[s]);
+        if (MODE == kDown) tma_load_2d(bt + bbytes, &maps.b_lo[hb], 64 * kb, p0, &k_full[s]);  // lo after hi
+      }
+    }
+  } else if (warp == 3 && lane == 0) {
+    // ---------------- weight producer: per raw stage the job's raw rows of
+    // kRawKB K-blocks (gate/up: with their scale bytes); per down job its
+    // 128 scale rows.  At the start of each job the next job's raw rows are
+    // prefetched into L2.
     auto prefetch_job = [&](int ux) {
       if (ux >= n_jobs) return;
       const int tx = ux / C::kSub, subx = ux % C::kSub;
@@ -370,142 +403,143 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
     };
     prefetch_job(blockIdx.x);
-    int it = 0;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
+    int rt = 0, jj = 0;
+    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       prefetch_job(u + gridDim.x);
       const int t = u / C::kSub, sub = u % C::kSub;
-      const int p0 = args.tile_p0[t], n = args.tile_n[t];
-      const int hb = n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3));
-      const uint32_t bbytes = (16u << hb) * 128u;
       const int blk = static_cast<int>(args.base + args.tile_e[t]);
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int sb = it % BS, sr = it % RS;
-        pf_wait(&b_empty[sb], ((it / BS) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&b_full[sb], (MODE == kDown ? 2 : 1) * bbytes);
-        uint8_t* bt = smem + L::kB + sb * C::kBMax;
-        tma_load_2d(bt, &maps.b[hb], 64 * kb, p0, &b_full[sb]);
-        if (MODE == kDown) tma_load_2d(bt + bbytes, &maps.b_lo[hb], 64 * kb, p0, &b_full[sb]);  // lo after hi
-        pf_wait(&r_empty[sr], ((it / RS) & 1) ^ 1, abort);
+      if (MODE == kDown) {  // the job's scale rows: [64 row pairs][80 B]
+        const int js = jj & 1;
+        pf_wait(&js_empty[js], ((jj >> 1) & 1) ^ 1, abort);
+        mbar_arrive_expect_tx(&js_full[js], C::kJobScales);
+        tma_load_3d(smem + L::kJs + js * C::kJobScales, &maps.s, 0, 64 * sub, blk, &js_full[js]);
+      }
+      for (int kb = 0; kb < KB; kb += C::kRawKB, ++rt) {
+        const int sr = rt % RS;
+        pf_wait(&r_empty[sr], ((rt / RS) & 1) ^ 1, abort);
         mbar_arrive_expect_tx(&r_full[sr], C::kRaw);
         uint8_t* raw = smem + L::kRaw + sr * C::kRaw;
-        if (MODE == kGateUp)
-          tma_load_4d(raw, &maps.w, 32 * kb, 128 * sub, 0, blk, &r_full[sr]);  // [gate|up][128][32 B]
-        else
-          tma_load_2d(raw, &maps.w, 32 * kb, blk * 8640 + 5120 + 128 * sub, &r_full[sr]);  // [128][32 B]
+        if (MODE == kGateUp) {  // [gate|up][128 rows][128 B] + [gate|up][128 rows][16 B of scales]
+          tma_load_4d(raw, &maps.w, 32 * kb, 128 * sub, 0, blk, &r_full[sr]);
+          tma_load_4d(raw + C::kRawBytes, &maps.s, 4 * kb, 128 * sub, 0, blk, &r_full[sr]);
+        } else {  // [128 rows][64 B]
+          tma_load_2d(raw, &maps.w, 32 * kb, blk * 8640 + 5120 + 128 * sub, &r_full[sr]);
+        }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    int it = 0, jj = 0;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
+  } else if ((warp == 1 || (MODE == kGateUp && warp == 2)) && lane == 0) {
+    // ---------------- MMA issuers.  Gate/up: warp 1 the gate accumulator,
+    // warp 2 the up accumulator (one thread issues ~one MMA per 44 cycles,
+    // so two issuers double the rate); down: warp 1.  Each issuer commits
+    // once per K-block (k_empty counts NI commits) and once per job.
+    const int g = warp - 1;  // 0: gate (or down), 1: up
+    int it = 0;
+    PfHalves hv;
+    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
       const int n = args.tile_n[u / C::kSub];
       const int rows = 16 << (n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)));  // activation box rows
       // gate/up: the tile's pairs (rounded up to 16); down: h hi rows then h lo rows of the box
       const int N = MODE == kDown ? 2 * rows : (n <= 16 ? 16 : (n + 15) & ~15);
       const uint32_t idesc = idesc_f16(128, N);
-      const int ab = jj & 1;
-      const uint32_t d0 = tmem + 256 * ab, d1 = d0 + 128;
-      pf_wait(&tm_empty[ab], ((jj >> 1) & 1) ^ 1, abort);
+      const int h = hv.pick(n);
+      if (h != 1) pf_wait(&tm_empty[0], (hv.u0 & 1) ^ 1, abort);
+      if (h != 0) pf_wait(&tm_empty[1], (hv.u1 & 1) ^ 1, abort);
       tc_fence_after();
+      const uint32_t d = tmem + (h == 1 ? 128u : 0u) + (g ? (h == 2 ? 128u : 64u) : 0u);
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int sb = it % BS, sa = it % AS;
-        pf_wait(&a_full[sa], (it / AS) & 1, abort);
-        pf_wait(&b_full[sb], (it / BS) & 1, abort);
+        const int s = it % KS;
+        pf_wait(&k_full[s], (it / KS) & 1, abort);
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + L::kA + sa * C::kABytes), a1 = a0 + 16384;
-        const uint32_t b0 = smem_u32(smem + L::kB + sb * C::kBMax);
+        const uint32_t a = tmem + kPfTmemA + 64 * s + 32 * g;
+        const uint32_t b0 = smem_u32(smem + L::kB + s * C::kBMax);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool acc = kb > 0 || k > 0;
-          const uint64_t bd = umma_desc_sw128(b0 + 32 * k, 1024);
-          mma_f16(d0, umma_desc_sw128(a0 + 32 * k, 1024), bd, idesc, acc);
-          if (MODE == kGateUp) mma_f16(d1, umma_desc_sw128(a1 + 32 * k, 1024), bd, idesc, acc);
-        }
-        mma_commit(&b_empty[sb]);
-        mma_commit(&a_empty[sa]);
+        for (int k = 0; k < 4; ++k)
+          mma_f16_ta(d, a + 8 * k, umma_desc_sw128(b0 + 32 * k, 1024), idesc, kb > 0 || k > 0);
+        mma_commit(&k_empty[s]);
       }
-      mma_commit(&tm_full[ab]);
+      if (h != 1) mma_commit(&tm_full[0]);
+      if (h != 0) mma_commit(&tm_full[1]);
+      hv.done(h);
     }
   } else if (warp >= 4 && warp < 12) {
-    // ---------------- dequantisers.  Gate/up: thread d builds row d % 128 of
-    // A tile d / 128 (the gate rows, then the up rows of the job's 128
-    // features), 64 k per K-block.  Down: threads 2r and 2r + 1 build output
-    // row r of the job's 128, 32 k each.
+    // ---------------- dequantisers: warp 4 + w writes TMEM lanes 32 (w % 4) ..
+    // of the A slot.  Gate/up: warps 4-7 the gate rows, warps 8-11 the up
+    // rows of the job's 128 features, 64 k per K-block.  Down: warps 4-7 the
+    // first 32 k, warps 8-11 the last 32 k of the job's 128 output rows.
     const int d = threadIdx.x - 128;
-    const int i = MODE == kGateUp ? d >> 7 : 0;
-    const int r = MODE == kGateUp ? (d & 127) : (d >> 1);
-    const int hf = MODE == kGateUp ? 0 : (d & 1);      // down: which half of the K-block
-    const uint32_t a_row = i * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
-    const int raw_off = MODE == kGateUp ? d * 32 : r * 32 + 16 * hf;
-    // Scale rows stream straight from global memory, three loads ahead of
-    // use, continuing across job boundaries.
-    auto sc_ptr = [&](int jjx, int g) -> const uint8_t* {
-      const int ux = blockIdx.x + jjx * gridDim.x;
-      if (ux >= n_jobs) return nullptr;
-      const int tx = ux / C::kSub, subx = ux % C::kSub;
-      const uint8_t* blkp = args.table + (args.base + args.tile_e[tx]) * kBlock;
-      if (MODE == kGateUp) return blkp + (i ? kOUS : kOGS) + (128 * subx + r) * (kHid / 16) + 16 * g;
-      return blkp + kODS + (128 * subx + r) * (kInter / 16) + 8 * g;
-    };
-    auto sc_load = [&](int lin) -> uint4 {
-      const uint8_t* p = sc_ptr(lin / C::kScGroups, lin % C::kScGroups);
-      if (!p) return make_uint4(0, 0, 0, 0);
-      if (MODE == kGateUp) return ldg_stream_v4(p);
-      const uint2 v = ldg_stream_v2(p);
-      return make_uint4(v.x, v.y, 0, 0);
-    };
-    uint4 q0 = sc_load(0), q1 = sc_load(1), q2 = sc_load(2), cur = q0;
+    const int i = d >> 7;                 // gate/up: which tile; down: which K half
+    const int r = d & 127;                // A row = TMEM lane
+    // raw row of this thread in a raw stage (gate/up: 128-byte rows, 128-byte
+    // swizzle; down: 64-byte rows, 64-byte swizzle)
+    const int raw_row = MODE == kGateUp ? d * 128 : r * 64;
+    const int swz = MODE == kGateUp ? (d & 7) : ((r >> 1) & 3);
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     int it = 0, jj = 0;
+    uint4 sc = make_uint4(0, 0, 0, 0);
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
+      const uint8_t* jsc = smem + L::kJs + (jj & 1) * C::kJobScales + r * (kInter / 16);
+      if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        if (kb % C::kScPerGroup == 0) {
-          const int lin = jj * C::kScGroups + kb / C::kScPerGroup;
-          cur = q0;
-          q0 = q1;
-          q1 = q2;
-          q2 = sc_load(lin + 3);
+        const int rt = it / C::kRawKB, sr = rt % RS, sa = it % KS;
+        const int kr = kb % C::kRawKB;  // K-block within the raw stage
+        const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
+        if (kr == 0) {
+          pf_wait(&r_full[sr], (rt / RS) & 1, abort);
+          if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
         }
-        const uint32_t sw = MODE == kGateUp ? pf_scale_word<MODE>(cur, kb) : ((kb & 1) ? cur.y : cur.x);
-        const int sr = it % RS, sa = it % AS;
-        pf_wait(&r_full[sr], (it / RS) & 1, abort);
-        pf_wait(&a_empty[sa], ((it / AS) & 1) ^ 1, abort);
-        const uint8_t* raw = smem + L::kRaw + sr * C::kRaw + raw_off;
-        uint8_t* a = smem + L::kA + sa * C::kABytes + a_row;
+        const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
+                                            : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
+        pf_wait(&k_empty[sa], ((it / KS) & 1) ^ 1, abort);
+        tc_fence_after();
+        const uint8_t* raw = stage + raw_row;
         uint32_t sa0, sa1, sa2, sa3;
         e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
         e4m3x2_to_bcast(sw >> 16, sa2, sa3);
+        const uint32_t acol = tmem + kPfTmemA + 64 * sa + lane_base;
         if (MODE == kGateUp) {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + 16);
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t h[4];
-            e2m1x8_to_f16x2(words[j], h);
-            const uint32_t sc2 = j < 2 ? sa0 : (j < 4 ? sa1 : (j < 6 ? sa2 : sa3));
-            const uint4 o = make_uint4(hmul2_u32(h[0], sc2), hmul2_u32(h[1], sc2), hmul2_u32(h[2], sc2),
-                                       hmul2_u32(h[3], sc2));
-            *reinterpret_cast<uint4*>(a + ((j ^ (r & 7)) << 4)) = o;
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t v[16];
+#pragma unroll
+            for (int jq = 0; jq < 4; ++jq) {
+              const int j = 4 * hh + jq;
+              uint32_t hf[4];
+              e2m1x8_to_f16x2(words[j], hf);
+              const uint32_t sc2 = j < 2 ? sa0 : (j < 4 ? sa1 : (j < 6 ? sa2 : sa3));
+              v[4 * jq + 0] = hmul2_u32(hf[0], sc2);
+              v[4 * jq + 1] = hmul2_u32(hf[1], sc2);
+              v[4 * jq + 2] = hmul2_u32(hf[2], sc2);
+              v[4 * jq + 3] = hmul2_u32(hf[3], sc2);
+            }
+            tmem_st_x16(acol + 32 * i + 16 * hh, v);
           }
         } else {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw);
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
           const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
-          const uint32_t s0 = hf ? sa2 : sa0, s1 = hf ? sa3 : sa1;
+          const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
+          uint32_t v[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            uint32_t h[4];
-            e2m1x8_to_f16x2(words[j], h);
+            uint32_t hf[4];
+            e2m1x8_to_f16x2(words[j], hf);
             const uint32_t sc2 = j < 2 ? s0 : s1;
-            const uint4 o = make_uint4(hmul2_u32(h[0], sc2), hmul2_u32(h[1], sc2), hmul2_u32(h[2], sc2),
-                                       hmul2_u32(h[3], sc2));
-            *reinterpret_cast<uint4*>(a + (((4 * hf + j) ^ (r & 7)) << 4)) = o;
+            v[4 * j + 0] = hmul2_u32(hf[0], sc2);
+            v[4 * j + 1] = hmul2_u32(hf[1], sc2);
+            v[4 * j + 2] = hmul2_u32(hf[2], sc2);
+            v[4 * j + 3] = hmul2_u32(hf[3], sc2);
           }
+          tmem_st_x16(acol + 16 * i, v);
         }
-        fence_proxy_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&a_full[sa]);
-          mbar_arrive(&r_empty[sr]);
+          mbar_arrive(&k_full[sa]);
+          if (kr == C::kRawKB - 1) mbar_arrive(&r_empty[sr]);
+          if (MODE == kDown && kb == KB - 1) mbar_arrive(&js_empty[jj & 1]);
         }
       }
     }
@@ -514,21 +548,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int q = warp - 12;
     const int et = threadIdx.x - 384;  // 0..127
     int jj = 0;
+    PfHalves hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       const int t = u / C::kSub, sub = u % C::kSub;
       const int e = args.tile_e[t], p0 = args.tile_p0[t], n = args.tile_n[t];
-      const int ab = jj & 1;
-      int* ccol = cols + ab * 3 * 128;
+      int* ccol = cols + (jj & 1) * 3 * 128;
       if (et < n) {
         ccol[et] = args.pair_tok[p0 + et];
         ccol[128 + et] = __float_as_int(args.pair_w[p0 + et]);
         ccol[256 + et] = args.pair_ex[p0 + et];
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      pf_wait(&tm_full[ab], (jj >> 1) & 1, abort);
+      const int h = hv.pick(n);
+      if (h != 1) pf_wait(&tm_full[0], hv.u0 & 1, abort);
+      if (h != 0) pf_wait(&tm_full[1], hv.u1 & 1, abort);
       tc_fence_after();
-      const uint32_t t0 = tmem + 256 * ab + (static_cast<uint32_t>(32 * q) << 16), t1 = t0 + 128;
+      const uint32_t t0 = tmem + (static_cast<uint32_t>(32 * q) << 16) + (h == 1 ? 128u : 0u);
       if (MODE == kGateUp) {
+        const uint32_t t1 = t0 + (h == 2 ? 128u : 64u);
         const float ws_g = args.s2l[3 * e + 0], ws_u = args.s2l[3 * e + 1];
         float* hrow = args.h32 + 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 32) {
@@ -542,7 +579,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               const int ex = ccol[256 + col];
               const float g = pow2_mul(__uint_as_float(vg[c]), -ex) * ws_g;
               const float uu = pow2_mul(__uint_as_float(vu[c]), -ex) * ws_u;
-              hrow[static_cast<int64_t>(p0 + col) * kInter] = g / (1.0f + expf(-g)) * uu;
+              hrow[static_cast<int64_t>(p0 + col) * kInter] = __fdividef(g, 1.0f + __expf(-g)) * uu;
             }
           }
         }
@@ -567,7 +604,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_before();
       asm volatile("bar.sync 1, 128;" ::: "memory");  // per-column data is reused two jobs later
-      if (lane == 0) mbar_arrive(&tm_empty[ab]);
+      if (lane == 0) {
+        if (h != 1) mbar_arrive(&tm_empty[0]);
+        if (h != 0) mbar_arrive(&tm_empty[1]);
+      }
+      hv.done(h);
     }
   }
   tc_fence_before();
@@ -709,13 +750,30 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   {  // gate and up rows of a block: [block][gate|up][640 rows][1280 B]
     const uint64_t dims[4] = {1280, 640, 2, static_cast<uint64_t>(n_blocks)};
     const uint64_t strides[3] = {1280, 819200, static_cast<uint64_t>(kBlock)};
-    const uint32_t box[4] = {32, 128, 2, 1};
-    if ((rc = tensor_map_nd(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, dims, strides, box, dev->device, &gu_maps.w)))
+    const uint32_t box[4] = {128, 128, 2, 1};
+    if ((rc = tensor_map_nd(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, dims, strides, box, dev->device, &gu_maps.w,
+                            CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
   }
-  if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 320, n_blocks * 8640, 320, 32, 128,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, dev->device, &dn_maps.w)))
+  if ((rc = tensor_map_2d(table, CU_TENSOR_MAP_DATA_TYPE_UINT8, 320, n_blocks * 8640, 320, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_64B, dev->device, &dn_maps.w)))
     return rc;
+  {  // gate and up scale rows: [block][gate|up][640 rows][160 B]; a box is 16 B (4 K-blocks) of 128 rows of both
+    const uint64_t dims[4] = {160, 640, 2, static_cast<uint64_t>(n_blocks)};
+    const uint64_t strides[3] = {160, static_cast<uint64_t>(kOUS - kOGS), static_cast<uint64_t>(kBlock)};
+    const uint32_t box[4] = {16, 128, 2, 1};
+    if ((rc = tensor_map_nd(table + kOGS, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, dims, strides, box, dev->device,
+                            &gu_maps.s)))
+      return rc;
+  }
+  {  // down scale rows as row pairs: [block][1280 pairs][80 B]; a box is a job's 128 rows
+    const uint64_t dims[3] = {80, 1280, static_cast<uint64_t>(n_blocks)};
+    const uint64_t strides[2] = {80, static_cast<uint64_t>(kBlock)};
+    const uint32_t box[3] = {80, 64, 1};
+    if ((rc = tensor_map_nd(table + kODS, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, dims, strides, box, dev->device,
+                            &dn_maps.s)))
+      return rc;
+  }
 
   // 3. gate/up
   PfArgs a{hdr, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, table, base, s2l, h32, out};
