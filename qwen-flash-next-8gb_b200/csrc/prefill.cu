@@ -215,7 +215,7 @@ enum { kGateUp = 0, kDown = 1 };
 // A job is (tile of <= 128 pairs, 128 weight rows): gate/up jobs take 128
 // features (their 128 gate rows and 128 up rows: two M = 128 accumulators
 // that hold g and u of the same feature in the same TMEM lane); down jobs
-// take 128 output rows.
+// take 128 output rows.  The K loop runs in stages of two K-blocks of 64.
 template <int MODE>
 struct PfCfg;
 template <>
@@ -224,10 +224,11 @@ struct PfCfg<kGateUp> {
   static constexpr int kRawKB = 4;              // K-blocks per raw stage: [gate|up][128 rows][128 B], 128-byte swizzle
   static constexpr int kKBlocks = kHid / 64;    // 40 K-blocks of 64
   static constexpr int kSub = kInter / 128;     // 5 jobs (128 features) per tile
-  static constexpr int kBMax = 16384;           // x tile: <= 128 rows x 64 f16
+  static constexpr int kBMax = 2 * 16384;       // x tile: 2 K-blocks of <= 128 rows x 64 f16
   static constexpr int kRawBytes = 32768;
   static constexpr int kRaw = kRawBytes + 4096;  // + [gate|up][128 rows][16 B] scales of the stage's 4 K-blocks
   static constexpr int kJobScales = 0;
+  static constexpr uint32_t kASlot = 128;       // TMEM columns per A slot: per K-block gate 32 + up 32
 };
 template <>
 struct PfCfg<kDown> {
@@ -235,18 +236,22 @@ struct PfCfg<kDown> {
   static constexpr int kRawKB = 2;              // [128 rows][64 B], 64-byte swizzle
   static constexpr int kKBlocks = kInter / 64;  // 10
   static constexpr int kSub = kHid / 128;       // 20 jobs (128 output rows) per tile
-  static constexpr int kBMax = 32768;           // h hi rows, then h lo rows (one MMA: N = 2 x box rows)
+  static constexpr int kBMax = 4 * 16384;       // per K-block: h hi rows, then h lo rows
   static constexpr int kRawBytes = 8192;
   static constexpr int kRaw = kRawBytes;
   static constexpr int kJobScales = 128 * (kInter / 16);  // a job's 128 scale rows of 40 B, loaded once per job
+  static constexpr uint32_t kASlot = 64;        // per K-block 32 columns
 };
-// TMEM: columns [0, 256) hold the accumulators as two halves of 128 columns;
-// a job with <= 64 pairs takes one half (gate/up: g in 64 columns, u in the
-// next 64; down: N = 2 x box rows <= 128), so its epilogue overlaps the next
-// job's MMAs in the other half; a larger job takes both.  Columns
-// [256, 512) are a ring of 4 dequantised A slots of 64 columns (a 128-row x
-// 64-k f16 tile is 32 columns; gate/up jobs use both halves of a slot).
-constexpr int kPfKStages = 4;  // K-block stages: activation tiles in shared memory, A slots in TMEM
+// Stages: activation tiles in shared memory and A slots in TMEM, two K-blocks each.
+constexpr int kPfKStages = 2;
+constexpr int kPfStageKB = 2;
+// TMEM: columns [0, 256) hold the accumulators as two halves of 128 columns.
+// Down jobs always take one half (a tile of <= 64 pairs: N = hi rows + lo
+// rows of the box; larger tiles: hi and lo MMAs into the same N = 128
+// accumulator); gate/up jobs of <= 64 pairs take one half (g in 64
+// columns, u in the next 64), larger ones both.  A job in one half has its
+// epilogue overlapped with the next job's MMAs.  Columns [256, 512) hold the
+// dequantised A slots.
 constexpr uint32_t kPfTmemA = 256;
 
 template <int MODE>
@@ -297,13 +302,14 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
-// Accumulator halves in use: the MMA issuer and the epilogue walk the same
+// Accumulator halves in use: the MMA issuers and the epilogue walk the same
 // job sequence and keep identical copies of this state.
+template <int MODE>
 struct PfHalves {
   uint32_t u0 = 0u, u1 = 0u;  // jobs that used half 0 / half 1 so far
   int next = 0;
   // the half a job of n pairs takes (2 = both)
-  __device__ __forceinline__ int pick(int n) const { return n > 64 ? 2 : next; }
+  __device__ __forceinline__ int pick(int n) const { return (MODE == kGateUp && n > 64) ? 2 : next; }
   __device__ __forceinline__ void done(int h) {
     if (h != 1) ++u0;
     if (h != 0) ++u1;
@@ -311,16 +317,19 @@ struct PfHalves {
   }
 };
 
+__device__ __forceinline__ int pf_box(int n) { return n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)); }
+
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
     pf_gemm_kernel(const __grid_constant__ PfMaps maps, const PfArgs args) {
   using C = PfCfg<MODE>;
   using L = PfSmem<MODE>;
-  constexpr int KS = kPfKStages, RS = C::kRStages, KB = C::kKBlocks;
+  constexpr int KS = kPfKStages, SK = kPfStageKB, RS = C::kRStages, KB = C::kKBlocks, NST = KB / SK;
   constexpr int NI = MODE == kGateUp ? 2 : 1;  // MMA issuers (gate/up: one for the gate rows, one for the up rows)
+  static_assert(KB % SK == 0 && C::kRawKB % SK == 0 || SK % C::kRawKB == 0, "stage / raw stage sizes");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  // K-block stage s: activation tile s in shared memory + A slot s in TMEM.
+  // stage s: activation tile s in shared memory + A slot s in TMEM.
   uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 8 dequant warps
   uint64_t* k_empty = k_full + KS;   // NI MMA issuers (commit)
   uint64_t* r_full = k_empty + KS;
@@ -368,22 +377,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int n_jobs = args.hdr[0] * C::kSub;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- activation producer: per K-block the tile's activation
-    // rows (two tiles for down: h hi, h lo) in the smallest box that holds
-    // them, completing on the stage's k_full barrier.
-    int it = 0;
+    // ---------------- activation producer: per stage the tile's activation
+    // rows of two K-blocks (down: h hi and h lo per K-block) in the smallest
+    // box that holds them, completing on the stage's k_full barrier.
+    int st = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
       const int t = u / C::kSub;
-      const int p0 = args.tile_p0[t], n = args.tile_n[t];
-      const int hb = n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3));
+      const int p0 = args.tile_p0[t], hb = pf_box(args.tile_n[t]);
       const uint32_t bbytes = (16u << hb) * 128u;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % KS;
-        pf_wait(&k_empty[s], ((it / KS) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&k_full[s], (MODE == kDown ? 2 : 1) * bbytes);
+      for (int q = 0; q < NST; ++q, ++st) {
+        const int s = st % KS;
+        pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
+        mbar_arrive_expect_tx(&k_full[s], (MODE == kDown ? 2 : 1) * SK * bbytes);
         uint8_t* bt = smem + L::kB + s * C::kBMax;
-        tma_load_2d(bt, &maps.b[hb], 64 * kb, p0, &k_full[s]);
-        if (MODE == kDown) tma_load_2d(bt + bbytes, &maps.b_lo[hb], 64 * kb, p0, &k_full[s]);  // lo after hi
+#pragma unroll
+        for (int j = 0; j < SK; ++j) {
+          const int kb = SK * q + j;
+          if (MODE == kGateUp) {
+            tma_load_2d(bt + j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
+          } else {  // [hi rows][lo rows] per K-block
+            tma_load_2d(bt + 2 * j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
+            tma_load_2d(bt + (2 * j + 1) * bbytes, &maps.b_lo[hb], 64 * kb, p0, &k_full[s]);
+          }
+        }
       }
     }
   } else if (warp == 3 && lane == 0) {
@@ -431,30 +447,41 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ---------------- MMA issuers.  Gate/up: warp 1 the gate accumulator,
     // warp 2 the up accumulator (one thread issues ~one MMA per 44 cycles,
     // so two issuers double the rate); down: warp 1.  Each issuer commits
-    // once per K-block (k_empty counts NI commits) and once per job.
+    // once per stage (k_empty counts NI commits) and once per job.
     const int g = warp - 1;  // 0: gate (or down), 1: up
-    int it = 0;
-    PfHalves hv;
+    int st = 0;
+    PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
       const int n = args.tile_n[u / C::kSub];
-      const int rows = 16 << (n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)));  // activation box rows
-      // gate/up: the tile's pairs (rounded up to 16); down: h hi rows then h lo rows of the box
-      const int N = MODE == kDown ? 2 * rows : (n <= 16 ? 16 : (n + 15) & ~15);
+      const int hb = pf_box(n), rows = 16 << hb;
+      const uint32_t bbytes = static_cast<uint32_t>(rows) * 128u;
+      // gate/up: the tile's pairs (rounded up to 16); down: hi rows then lo rows
+      // of the box in one MMA, or (128-row box) hi and lo in two MMAs
+      const bool split = MODE == kDown && rows == 128;
+      const int N = MODE == kDown ? (split ? 128 : 2 * rows) : (n <= 16 ? 16 : (n + 15) & ~15);
       const uint32_t idesc = idesc_f16(128, N);
       const int h = hv.pick(n);
       if (h != 1) pf_wait(&tm_empty[0], (hv.u0 & 1) ^ 1, abort);
       if (h != 0) pf_wait(&tm_empty[1], (hv.u1 & 1) ^ 1, abort);
       tc_fence_after();
       const uint32_t d = tmem + (h == 1 ? 128u : 0u) + (g ? (h == 2 ? 128u : 64u) : 0u);
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % KS;
-        pf_wait(&k_full[s], (it / KS) & 1, abort);
+      for (int q = 0; q < NST; ++q, ++st) {
+        const int s = st % KS;
+        pf_wait(&k_full[s], (st / KS) & 1, abort);
         tc_fence_after();
-        const uint32_t a = tmem + kPfTmemA + 64 * s + 32 * g;
+        const uint32_t a = tmem + kPfTmemA + C::kASlot * s + 32 * g;
         const uint32_t b0 = smem_u32(smem + L::kB + s * C::kBMax);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f16_ta(d, a + 8 * k, umma_desc_sw128(b0 + 32 * k, 1024), idesc, kb > 0 || k > 0);
+        for (int j = 0; j < SK; ++j) {
+          const uint32_t aj = a + (MODE == kGateUp ? 64u : 32u) * j;
+          const uint32_t bj = b0 + (MODE == kDown ? 2u : 1u) * j * bbytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const bool acc = q > 0 || j > 0 || k > 0;
+            mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + 32 * k, 1024), idesc, acc);
+            if (split) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + bbytes + 32 * k, 1024), idesc, true);
+          }
+        }
         mma_commit(&k_empty[s]);
       }
       if (h != 1) mma_commit(&tm_full[0]);
@@ -465,7 +492,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ---------------- dequantisers: warp 4 + w writes TMEM lanes 32 (w % 4) ..
     // of the A slot.  Gate/up: warps 4-7 the gate rows, warps 8-11 the up
     // rows of the job's 128 features, 64 k per K-block.  Down: warps 4-7 the
-    // first 32 k, warps 8-11 the last 32 k of the job's 128 output rows.
+    // first 32 k, warps 8-11 the last 32 k of each K-block of the job's 128
+    // output rows.
     const int d = threadIdx.x - 128;
     const int i = d >> 7;                 // gate/up: which tile; down: which K half
     const int r = d & 127;                // A row = TMEM lane
@@ -474,72 +502,77 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int raw_row = MODE == kGateUp ? d * 128 : r * 64;
     const int swz = MODE == kGateUp ? (d & 7) : ((r >> 1) & 3);
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    int it = 0, jj = 0;
+    int st = 0, jj = 0;
     uint4 sc = make_uint4(0, 0, 0, 0);
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       const uint8_t* jsc = smem + L::kJs + (jj & 1) * C::kJobScales + r * (kInter / 16);
       if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int rt = it / C::kRawKB, sr = rt % RS, sa = it % KS;
-        const int kr = kb % C::kRawKB;  // K-block within the raw stage
-        const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
-        if (kr == 0) {
-          pf_wait(&r_full[sr], (rt / RS) & 1, abort);
-          if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
-        }
-        const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
-                                            : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
-        pf_wait(&k_empty[sa], ((it / KS) & 1) ^ 1, abort);
+      for (int q = 0; q < NST; ++q, ++st) {
+        const int s = st % KS;
+        pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
         tc_fence_after();
-        const uint8_t* raw = stage + raw_row;
-        uint32_t sa0, sa1, sa2, sa3;
-        e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
-        e4m3x2_to_bcast(sw >> 16, sa2, sa3);
-        const uint32_t acol = tmem + kPfTmemA + 64 * sa + lane_base;
-        if (MODE == kGateUp) {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
-          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
-          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + lane_base;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t v[16];
+        for (int j = 0; j < SK; ++j) {
+          const int kb = SK * q + j;
+          const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
+          const int rt = gkb / C::kRawKB, sr = rt % RS;
+          const int kr = kb % C::kRawKB;  // K-block within the raw stage
+          const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
+          if (kr == 0) {
+            pf_wait(&r_full[sr], (rt / RS) & 1, abort);
+            if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
+          }
+          const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
+                                              : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
+          const uint8_t* raw = stage + raw_row;
+          uint32_t sa0, sa1, sa2, sa3;
+          e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
+          e4m3x2_to_bcast(sw >> 16, sa2, sa3);
+          if (MODE == kGateUp) {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
+            const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            uint32_t v[32];
 #pragma unroll
-            for (int jq = 0; jq < 4; ++jq) {
-              const int j = 4 * hh + jq;
+            for (int jq = 0; jq < 8; ++jq) {
               uint32_t hf[4];
-              e2m1x8_to_f16x2(words[j], hf);
-              const uint32_t sc2 = j < 2 ? sa0 : (j < 4 ? sa1 : (j < 6 ? sa2 : sa3));
+              e2m1x8_to_f16x2(words[jq], hf);
+              const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
               v[4 * jq + 0] = hmul2_u32(hf[0], sc2);
               v[4 * jq + 1] = hmul2_u32(hf[1], sc2);
               v[4 * jq + 2] = hmul2_u32(hf[2], sc2);
               v[4 * jq + 3] = hmul2_u32(hf[3], sc2);
             }
-            tmem_st_x16(acol + 32 * i + 16 * hh, v);
-          }
-        } else {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
-          const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
-          const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
-          uint32_t v[16];
+            tmem_st_x32(aslot + 64 * j + 32 * i, v);
+          } else {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
+            const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
+            const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
+            uint32_t v[16];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t hf[4];
-            e2m1x8_to_f16x2(words[j], hf);
-            const uint32_t sc2 = j < 2 ? s0 : s1;
-            v[4 * j + 0] = hmul2_u32(hf[0], sc2);
-            v[4 * j + 1] = hmul2_u32(hf[1], sc2);
-            v[4 * j + 2] = hmul2_u32(hf[2], sc2);
-            v[4 * j + 3] = hmul2_u32(hf[3], sc2);
+            for (int jq = 0; jq < 4; ++jq) {
+              uint32_t hf[4];
+              e2m1x8_to_f16x2(words[jq], hf);
+              const uint32_t sc2 = jq < 2 ? s0 : s1;
+              v[4 * jq + 0] = hmul2_u32(hf[0], sc2);
+              v[4 * jq + 1] = hmul2_u32(hf[1], sc2);
+              v[4 * jq + 2] = hmul2_u32(hf[2], sc2);
+              v[4 * jq + 3] = hmul2_u32(hf[3], sc2);
+            }
+            tmem_st_x16(aslot + 32 * j + 16 * i, v);
           }
-          tmem_st_x16(acol + 16 * i, v);
+          if (kr == C::kRawKB - 1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[sr]);
+          }
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&k_full[sa]);
-          if (kr == C::kRawKB - 1) mbar_arrive(&r_empty[sr]);
-          if (MODE == kDown && kb == KB - 1) mbar_arrive(&js_empty[jj & 1]);
+          mbar_arrive(&k_full[s]);
+          if (MODE == kDown && q == NST - 1) mbar_arrive(&js_empty[jj & 1]);
         }
       }
     }
@@ -548,7 +581,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int q = warp - 12;
     const int et = threadIdx.x - 384;  // 0..127
     int jj = 0;
-    PfHalves hv;
+    PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       const int t = u / C::kSub, sub = u % C::kSub;
       const int e = args.tile_e[t], p0 = args.tile_p0[t], n = args.tile_n[t];
@@ -577,27 +610,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int col = c0 + c;
             if (col < n) {
               const int ex = ccol[256 + col];
-              const float g = pow2_mul(__uint_as_float(vg[c]), -ex) * ws_g;
+              const float gg = pow2_mul(__uint_as_float(vg[c]), -ex) * ws_g;
               const float uu = pow2_mul(__uint_as_float(vu[c]), -ex) * ws_u;
-              hrow[static_cast<int64_t>(p0 + col) * kInter] = __fdividef(g, 1.0f + __expf(-g)) * uu;
+              hrow[static_cast<int64_t>(p0 + col) * kInter] = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
             }
           }
         }
       } else {
         const float ws_d = args.s2l[3 * e + 2];
-        const int rows = 16 << (n <= 16 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)));
+        const int rows = 16 << pf_box(n);
         const int row = 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 32) {
           uint32_t vh[32], vl[32];
           tmem_ld_x32(t0 + c0, vh);
-          tmem_ld_x32(t0 + rows + c0, vl);
+          if (rows < 128) tmem_ld_x32(t0 + rows + c0, vl);  // lo columns (128-row boxes: summed by the MMA)
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const int col = c0 + c;
             if (col < n) {
               const float f = pow2_mul(__int_as_float(ccol[128 + col]) * ws_d, -ccol[256 + col]);
-              atomicAdd(args.out + static_cast<int64_t>(ccol[col]) * kHid + row,
-                        (__uint_as_float(vh[c]) + __uint_as_float(vl[c])) * f);
+              const float v = rows < 128 ? __uint_as_float(vh[c]) + __uint_as_float(vl[c]) : __uint_as_float(vh[c]);
+              atomicAdd(args.out + static_cast<int64_t>(ccol[col]) * kHid + row, v * f);
             }
           }
         }
