@@ -391,6 +391,21 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, 
 }  // namespace qfn
 
 namespace qfn {
+// One lane of a converged warp (the same lane every call): the issuer of
+// TMA copies, MMAs and commits in warp-wide producer / MMA loops.  Keeping
+// the whole warp in the loop keeps descriptors and addresses in uniform
+// registers, which issues tcgen05 instructions about twice as fast as a
+// loop run by a single lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+}  // namespace qfn
+
+namespace qfn {
 // Prefetch `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

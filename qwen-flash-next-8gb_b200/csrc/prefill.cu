@@ -376,10 +376,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tmem = *tslot;
   const int n_jobs = args.hdr[0] * C::kSub;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- activation producer: per stage the tile's activation
-    // rows of two K-blocks (down: h hi and h lo per K-block) in the smallest
-    // box that holds them, completing on the stage's k_full barrier.
+  if (warp == 0) {
+    // ---------------- activation producer (warp 0; one elected lane issues):
+    // per stage the tile's activation rows of two K-blocks (down: h hi and
+    // h lo per K-block) in the smallest box that holds them, completing on
+    // the stage's k_full barrier.
     int st = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
       const int t = u / C::kSub;
@@ -388,22 +389,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int q = 0; q < NST; ++q, ++st) {
         const int s = st % KS;
         pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&k_full[s], (MODE == kDown ? 2 : 1) * SK * bbytes);
-        uint8_t* bt = smem + L::kB + s * C::kBMax;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&k_full[s], (MODE == kDown ? 2 : 1) * SK * bbytes);
+          uint8_t* bt = smem + L::kB + s * C::kBMax;
 #pragma unroll
-        for (int j = 0; j < SK; ++j) {
-          const int kb = SK * q + j;
-          if (MODE == kGateUp) {
-            tma_load_2d(bt + j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
-          } else {  // [hi rows][lo rows] per K-block
-            tma_load_2d(bt + 2 * j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
-            tma_load_2d(bt + (2 * j + 1) * bbytes, &maps.b_lo[hb], 64 * kb, p0, &k_full[s]);
+          for (int j = 0; j < SK; ++j) {
+            const int kb = SK * q + j;
+            if (MODE == kGateUp) {
+              tma_load_2d(bt + j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
+            } else {  // [hi rows][lo rows] per K-block
+              tma_load_2d(bt + 2 * j * bbytes, &maps.b[hb], 64 * kb, p0, &k_full[s]);
+              tma_load_2d(bt + (2 * j + 1) * bbytes, &maps.b_lo[hb], 64 * kb, p0, &k_full[s]);
+            }
           }
         }
+        __syncwarp();
       }
     }
-  } else if (warp == 3 && lane == 0) {
-    // ---------------- weight producer: per raw stage the job's raw rows of
+  } else if (warp == 3) {
+    // ---------------- weight producer (warp 3; one elected lane issues): per raw stage the job's raw rows of
     // kRawKB K-blocks (gate/up: with their scale bytes); per down job its
     // 128 scale rows.  At the start of each job the next job's raw rows are
     // prefetched into L2.
@@ -418,36 +422,42 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         bulk_prefetch_l2(blkp + kODW + 128 * subx * (kInter / 2), 128 * (kInter / 2));
       }
     };
-    prefetch_job(blockIdx.x);
+    if (elect_one()) prefetch_job(blockIdx.x);
     int rt = 0, jj = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
-      prefetch_job(u + gridDim.x);
+      if (elect_one()) prefetch_job(u + gridDim.x);
       const int t = u / C::kSub, sub = u % C::kSub;
       const int blk = static_cast<int>(args.base + args.tile_e[t]);
       if (MODE == kDown) {  // the job's scale rows: [64 row pairs][80 B]
         const int js = jj & 1;
         pf_wait(&js_empty[js], ((jj >> 1) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&js_full[js], C::kJobScales);
-        tma_load_3d(smem + L::kJs + js * C::kJobScales, &maps.s, 0, 64 * sub, blk, &js_full[js]);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&js_full[js], C::kJobScales);
+          tma_load_3d(smem + L::kJs + js * C::kJobScales, &maps.s, 0, 64 * sub, blk, &js_full[js]);
+        }
+        __syncwarp();
       }
       for (int kb = 0; kb < KB; kb += C::kRawKB, ++rt) {
         const int sr = rt % RS;
         pf_wait(&r_empty[sr], ((rt / RS) & 1) ^ 1, abort);
-        mbar_arrive_expect_tx(&r_full[sr], C::kRaw);
-        uint8_t* raw = smem + L::kRaw + sr * C::kRaw;
-        if (MODE == kGateUp) {  // [gate|up][128 rows][128 B] + [gate|up][128 rows][16 B of scales]
-          tma_load_4d(raw, &maps.w, 32 * kb, 128 * sub, 0, blk, &r_full[sr]);
-          tma_load_4d(raw + C::kRawBytes, &maps.s, 4 * kb, 128 * sub, 0, blk, &r_full[sr]);
-        } else {  // [128 rows][64 B]
-          tma_load_2d(raw, &maps.w, 32 * kb, blk * 8640 + 5120 + 128 * sub, &r_full[sr]);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&r_full[sr], C::kRaw);
+          uint8_t* raw = smem + L::kRaw + sr * C::kRaw;
+          if (MODE == kGateUp) {  // [gate|up][128 rows][128 B] + [gate|up][128 rows][16 B of scales]
+            tma_load_4d(raw, &maps.w, 32 * kb, 128 * sub, 0, blk, &r_full[sr]);
+            tma_load_4d(raw + C::kRawBytes, &maps.s, 4 * kb, 128 * sub, 0, blk, &r_full[sr]);
+          } else {  // [128 rows][64 B]
+            tma_load_2d(raw, &maps.w, 32 * kb, blk * 8640 + 5120 + 128 * sub, &r_full[sr]);
+          }
         }
+        __syncwarp();
       }
     }
-  } else if ((warp == 1 || (MODE == kGateUp && warp == 2)) && lane == 0) {
-    // ---------------- MMA issuers.  Gate/up: warp 1 the gate accumulator,
-    // warp 2 the up accumulator (one thread issues ~one MMA per 44 cycles,
-    // so two issuers double the rate); down: warp 1.  Each issuer commits
-    // once per stage (k_empty counts NI commits) and once per job.
+  } else if (warp == 1 || (MODE == kGateUp && warp == 2)) {
+    // ---------------- MMA issuers (one elected lane of the warp issues).
+    // Gate/up: warp 1 the gate accumulator, warp 2 the up accumulator (two
+    // issuers nearly double the MMA issue rate); down: warp 1.  Each issuer
+    // commits once per stage (k_empty counts NI commits) and once per job.
     const int g = warp - 1;  // 0: gate (or down), 1: up
     int st = 0;
     PfHalves<MODE> hv;
@@ -478,14 +488,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const bool acc = q > 0 || j > 0 || k > 0;
-            mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + 32 * k, 1024), idesc, acc);
-            if (split) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + bbytes + 32 * k, 1024), idesc, true);
+            if (elect_one()) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + 32 * k, 1024), idesc, acc);
+            if (split && elect_one()) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + bbytes + 32 * k, 1024), idesc, true);
           }
         }
-        mma_commit(&k_empty[s]);
+        if (elect_one()) mma_commit(&k_empty[s]);
+        __syncwarp();
       }
-      if (h != 1) mma_commit(&tm_full[0]);
-      if (h != 0) mma_commit(&tm_full[1]);
+      if (elect_one()) {
+        if (h != 1) mma_commit(&tm_full[0]);
+        if (h != 0) mma_commit(&tm_full[1]);
+      }
+      __syncwarp();
       hv.done(h);
     }
   } else if (warp >= 4 && warp < 12) {
