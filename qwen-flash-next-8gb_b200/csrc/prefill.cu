@@ -39,7 +39,7 @@
 namespace qfn {
 
 constexpr int kPfRows = 128;           // pairs per tile (MMA N <= 128) and A rows (MMA M)
-constexpr int kPfThreads = 512;
+constexpr int kPfThreads = 768;  // 24 warps: 2 producers, 2 MMA issuers, 16 dequantisers, 4 epilogue
 constexpr int kPfMaxExperts = 1024;
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
@@ -330,14 +330,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   // stage s: activation tile s in shared memory + A slot s in TMEM.
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 8 dequant warps
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 16 dequant warps
   uint64_t* k_empty = k_full + KS;   // NI MMA issuers (commit)
   uint64_t* r_full = k_empty + KS;
-  uint64_t* r_empty = r_full + RS;   // 8 dequant warps
+  uint64_t* r_empty = r_full + RS;   // 16 dequant warps
   uint64_t* tm_full = r_empty + RS;  // [2] accumulator halves: NI MMA issuers -> epilogue
   uint64_t* tm_empty = tm_full + 2;  // [2] 4 epilogue warps
   uint64_t* js_full = tm_empty + 2;  // [2] down: per-job scale rows
-  uint64_t* js_empty = js_full + 2;  // [2] 8 dequant warps
+  uint64_t* js_empty = js_full + 2;  // [2] 16 dequant warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(js_empty + 2);
   volatile uint32_t* abort = tslot + 1;
   int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][3][128]: token, weight bits, exponent
@@ -346,18 +346,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     *abort = 0u;
     for (int s = 0; s < KS; ++s) {
-      mbar_init(&k_full[s], 9);
+      mbar_init(&k_full[s], 17);
       mbar_init(&k_empty[s], NI);
     }
     for (int s = 0; s < RS; ++s) {
       mbar_init(&r_full[s], 1);
-      mbar_init(&r_empty[s], 8);
+      mbar_init(&r_empty[s], 16);
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&tm_full[h], NI);
       mbar_init(&tm_empty[h], 4);
       mbar_init(&js_full[h], 1);
-      mbar_init(&js_empty[h], 8);
+      mbar_init(&js_empty[h], 16);
     }
     fence_mbar_init();
   }
@@ -475,24 +475,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (h != 0) pf_wait(&tm_empty[1], (hv.u1 & 1) ^ 1, abort);
       tc_fence_after();
       const uint32_t d = tmem + (h == 1 ? 128u : 0u) + (g ? (h == 2 ? 128u : 64u) : 0u);
+      // B descriptors differ only in the start address field (address / 16):
+      // +2 per k-step of 16, +jstep per K-block, +lostep for the h lo rows.
+      const uint64_t bdesc0 = umma_desc_sw128(smem_u32(smem + L::kB), 1024);
+      const uint32_t jstep = ((MODE == kDown ? 2u : 1u) * bbytes) >> 4, lostep = bbytes >> 4;
       for (int q = 0; q < NST; ++q, ++st) {
         const int s = st % KS;
         pf_wait(&k_full[s], (st / KS) & 1, abort);
         tc_fence_after();
-        const uint32_t a = tmem + kPfTmemA + C::kASlot * s + 32 * g;
-        const uint32_t b0 = smem_u32(smem + L::kB + s * C::kBMax);
+        if (elect_one()) {
+          const uint32_t a = tmem + kPfTmemA + C::kASlot * s + 32 * g;
+          const uint64_t bd = bdesc0 + static_cast<uint32_t>((s * C::kBMax) >> 4);
 #pragma unroll
-        for (int j = 0; j < SK; ++j) {
-          const uint32_t aj = a + (MODE == kGateUp ? 64u : 32u) * j;
-          const uint32_t bj = b0 + (MODE == kDown ? 2u : 1u) * j * bbytes;
+          for (int j = 0; j < SK; ++j) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const bool acc = q > 0 || j > 0 || k > 0;
-            if (elect_one()) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + 32 * k, 1024), idesc, acc);
-            if (split && elect_one()) mma_f16_ta(d, aj + 8 * k, umma_desc_sw128(bj + bbytes + 32 * k, 1024), idesc, true);
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t ak = a + (MODE == kGateUp ? 64u : 32u) * j + 8 * k;
+              const uint64_t bk = bd + (j * jstep + 2 * k);
+              mma_f16_ta(d, ak, bk, idesc, (j | k) != 0 || q > 0);
+              if (split) mma_f16_ta(d, ak, bk + lostep, idesc, true);
+            }
           }
+          mma_commit(&k_empty[s]);
         }
-        if (elect_one()) mma_commit(&k_empty[s]);
         __syncwarp();
       }
       if (elect_one()) {
@@ -502,20 +507,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       hv.done(h);
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < 20) {
     // ---------------- dequantisers: warp 4 + w writes TMEM lanes 32 (w % 4) ..
-    // of the A slot.  Gate/up: warps 4-7 the gate rows, warps 8-11 the up
-    // rows of the job's 128 features, 64 k per K-block.  Down: warps 4-7 the
-    // first 32 k, warps 8-11 the last 32 k of each K-block of the job's 128
-    // output rows.
-    const int d = threadIdx.x - 128;
-    const int i = d >> 7;                 // gate/up: which tile; down: which K half
-    const int r = d & 127;                // A row = TMEM lane
+    // + 31 of the A slot, one K-block (j = w / 8) of the stage.  Gate/up:
+    // matrix i = (w / 4) % 2 (gate / up rows of the job's 128 features), 64 k;
+    // down: K half i = (w / 4) % 2 (32 k) of the job's 128 output rows.  A
+    // warp converts its K-block into registers before it waits for the A slot,
+    // so the conversion overlaps the MMAs of the previous stage.
+    const int w = warp - 4;
+    const int i = (w >> 2) & 1, j = w >> 3;
+    const int r = 32 * (w & 3) + lane;    // A row = TMEM lane
+    const int d = 128 * i + r;            // gate/up: row of the raw stage ([gate|up][128])
     // raw row of this thread in a raw stage (gate/up: 128-byte rows, 128-byte
     // swizzle; down: 64-byte rows, 64-byte swizzle)
     const int raw_row = MODE == kGateUp ? d * 128 : r * 64;
     const int swz = MODE == kGateUp ? (d & 7) : ((r >> 1) & 3);
-    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (w & 3)) << 16;
+    const uint32_t acol = (MODE == kGateUp ? 64u * j + 32u * i : 32u * j + 16u * i) + lane_base;
     int st = 0, jj = 0;
     uint4 sc = make_uint4(0, 0, 0, 0);
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
@@ -523,64 +531,57 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
       for (int q = 0; q < NST; ++q, ++st) {
         const int s = st % KS;
-        pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
-        tc_fence_after();
-        const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + lane_base;
+        const int kb = SK * q + j;
+        const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
+        const int rt = gkb / C::kRawKB, sr = rt % RS;
+        const int kr = kb % C::kRawKB;  // K-block within the raw stage
+        const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
+        if (kr < SK) {  // this warp's first K-block of the raw stage
+          pf_wait(&r_full[sr], (rt / RS) & 1, abort);
+          if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
+        }
+        const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
+                                            : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
+        const uint8_t* raw = stage + raw_row;
+        uint32_t sa0, sa1, sa2, sa3;
+        e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
+        e4m3x2_to_bcast(sw >> 16, sa2, sa3);
+        constexpr int NV = MODE == kGateUp ? 32 : 16;
+        uint32_t v[NV];
+        if (MODE == kGateUp) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
+          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int j = 0; j < SK; ++j) {
-          const int kb = SK * q + j;
-          const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
-          const int rt = gkb / C::kRawKB, sr = rt % RS;
-          const int kr = kb % C::kRawKB;  // K-block within the raw stage
-          const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
-          if (kr == 0) {
-            pf_wait(&r_full[sr], (rt / RS) & 1, abort);
-            if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
+          for (int jq = 0; jq < 8; ++jq) {
+            uint32_t hf[4];
+            e2m1x8_to_f16x2(words[jq], hf);
+            const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[(4 * jq + e) % NV] = hmul2_u32(hf[e], sc2);
           }
-          const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
-                                              : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
-          const uint8_t* raw = stage + raw_row;
-          uint32_t sa0, sa1, sa2, sa3;
-          e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
-          e4m3x2_to_bcast(sw >> 16, sa2, sa3);
-          if (MODE == kGateUp) {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
-            const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
-            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            uint32_t v[32];
+        } else {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
+          const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
 #pragma unroll
-            for (int jq = 0; jq < 8; ++jq) {
-              uint32_t hf[4];
-              e2m1x8_to_f16x2(words[jq], hf);
-              const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
-              v[4 * jq + 0] = hmul2_u32(hf[0], sc2);
-              v[4 * jq + 1] = hmul2_u32(hf[1], sc2);
-              v[4 * jq + 2] = hmul2_u32(hf[2], sc2);
-              v[4 * jq + 3] = hmul2_u32(hf[3], sc2);
-            }
-            tmem_st_x32(aslot + 64 * j + 32 * i, v);
-          } else {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
-            const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
-            const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
-            uint32_t v[16];
+          for (int jq = 0; jq < 4; ++jq) {
+            uint32_t hf[4];
+            e2m1x8_to_f16x2(words[jq], hf);
+            const uint32_t sc2 = jq < 2 ? s0 : s1;
 #pragma unroll
-            for (int jq = 0; jq < 4; ++jq) {
-              uint32_t hf[4];
-              e2m1x8_to_f16x2(words[jq], hf);
-              const uint32_t sc2 = jq < 2 ? s0 : s1;
-              v[4 * jq + 0] = hmul2_u32(hf[0], sc2);
-              v[4 * jq + 1] = hmul2_u32(hf[1], sc2);
-              v[4 * jq + 2] = hmul2_u32(hf[2], sc2);
-              v[4 * jq + 3] = hmul2_u32(hf[3], sc2);
-            }
-            tmem_st_x16(aslot + 32 * j + 16 * i, v);
-          }
-          if (kr == C::kRawKB - 1) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&r_empty[sr]);
+            for (int e = 0; e < 4; ++e) v[4 * jq + e] = hmul2_u32(hf[e], sc2);
           }
         }
+        if (kr >= C::kRawKB - SK) {  // this warp's last K-block of the raw stage: release it
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&r_empty[sr]);
+        }
+        pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
+        tc_fence_after();
+        const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + acol;
+        if (MODE == kGateUp) tmem_st_x32(aslot, *reinterpret_cast<uint32_t(*)[32]>(v));
+        else tmem_st_x16(aslot, *reinterpret_cast<uint32_t(*)[16]>(v));
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -590,10 +591,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
     }
-  } else if (warp >= 12) {
-    // ---------------- epilogue: warp 12 + q reads TMEM lanes 32q .. 32q + 31
-    const int q = warp - 12;
-    const int et = threadIdx.x - 384;  // 0..127
+  } else if (warp >= 20) {
+    // ---------------- epilogue: warp 20 + q reads TMEM lanes 32q .. 32q + 31
+    const int q = warp - 20;
+    const int et = threadIdx.x - 640;  // 0..127
     int jj = 0;
     PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
@@ -615,12 +616,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t t1 = t0 + (h == 2 ? 128u : 64u);
         const float ws_g = args.s2l[3 * e + 0], ws_u = args.s2l[3 * e + 1];
         float* hrow = args.h32 + 128 * sub + 32 * q + lane;
-        for (int c0 = 0; c0 < n; c0 += 32) {
-          uint32_t vg[32], vu[32];
-          tmem_ld_x32(t0 + c0, vg);
-          tmem_ld_x32(t1 + c0, vu);
+        for (int c0 = 0; c0 < n; c0 += 16) {
+          uint32_t vg[16], vu[16];
+          tmem_ld_x16(t0 + c0, vg);
+          tmem_ld_x16(t1 + c0, vu);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
+          for (int c = 0; c < 16; ++c) {
             const int col = c0 + c;
             if (col < n) {
               const int ex = ccol[256 + col];
@@ -634,12 +635,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const float ws_d = args.s2l[3 * e + 2];
         const int rows = 16 << pf_box(n);
         const int row = 128 * sub + 32 * q + lane;
-        for (int c0 = 0; c0 < n; c0 += 32) {
-          uint32_t vh[32], vl[32];
-          tmem_ld_x32(t0 + c0, vh);
-          if (rows < 128) tmem_ld_x32(t0 + rows + c0, vl);  // lo columns (128-row boxes: summed by the MMA)
+        for (int c0 = 0; c0 < n; c0 += 16) {
+          uint32_t vh[16], vl[16];
+          tmem_ld_x16(t0 + c0, vh);
+          if (rows < 128) tmem_ld_x16(t0 + rows + c0, vl);  // lo columns (128-row boxes: summed by the MMA)
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
+          for (int c = 0; c < 16; ++c) {
             const int col = c0 + c;
             if (col < n) {
               const float f = pow2_mul(__int_as_float(ccol[128 + col]) * ws_d, -ccol[256 + col]);
