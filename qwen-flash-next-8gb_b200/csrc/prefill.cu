@@ -39,7 +39,7 @@
 namespace qfn {
 
 constexpr int kPfRows = 128;           // pairs per tile (MMA N <= 128) and A rows (MMA M)
-constexpr int kPfThreads = 768;  // 24 warps: 2 producers, 2 MMA issuers, 16 dequantisers, 4 epilogue
+constexpr int kPfThreads = 512;  // 16 warps: 2 producers, 2 MMA issuers, 8 dequantisers, 4 epilogue
 constexpr int kPfMaxExperts = 1024;
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
@@ -212,6 +212,13 @@ __global__ void __launch_bounds__(160) pf_hpack_kernel(const float* __restrict__
 
 enum { kGateUp = 0, kDown = 1 };
 
+#ifndef PF_GU_SK
+#define PF_GU_SK 2
+#endif
+#ifndef PF_DN_SK
+#define PF_DN_SK 2
+#endif
+
 // A job is (tile of <= 128 pairs, 128 weight rows): gate/up jobs take 128
 // features (their 128 gate rows and 128 up rows: two M = 128 accumulators
 // that hold g and u of the same feature in the same TMEM lane); down jobs
@@ -224,11 +231,13 @@ struct PfCfg<kGateUp> {
   static constexpr int kRawKB = 4;              // K-blocks per raw stage: [gate|up][128 rows][128 B], 128-byte swizzle
   static constexpr int kKBlocks = kHid / 64;    // 40 K-blocks of 64
   static constexpr int kSub = kInter / 128;     // 5 jobs (128 features) per tile
-  static constexpr int kBMax = 2 * 16384;       // x tile: 2 K-blocks of <= 128 rows x 64 f16
+  static constexpr int kStageKB = PF_GU_SK;     // K-blocks per stage
+  static constexpr int kKStages = 4 / PF_GU_SK;  // stages in flight (A slots: 256 TMEM columns)
+  static constexpr int kBMax = kStageKB * 16384;  // x tile per K-block: <= 128 rows x 64 f16
   static constexpr int kRawBytes = 32768;
   static constexpr int kRaw = kRawBytes + 4096;  // + [gate|up][128 rows][16 B] scales of the stage's 4 K-blocks
   static constexpr int kJobScales = 0;
-  static constexpr uint32_t kASlot = 128;       // TMEM columns per A slot: per K-block gate 32 + up 32
+  static constexpr uint32_t kASlot = 64 * kStageKB;  // TMEM columns per A slot: per K-block gate 32 + up 32
 };
 template <>
 struct PfCfg<kDown> {
@@ -236,15 +245,15 @@ struct PfCfg<kDown> {
   static constexpr int kRawKB = 2;              // [128 rows][64 B], 64-byte swizzle
   static constexpr int kKBlocks = kInter / 64;  // 10
   static constexpr int kSub = kHid / 128;       // 20 jobs (128 output rows) per tile
-  static constexpr int kBMax = 4 * 16384;       // per K-block: h hi rows, then h lo rows
+  static constexpr int kStageKB = PF_DN_SK;
+  static constexpr int kKStages = 4 / PF_DN_SK;
+  static constexpr int kBMax = kStageKB * 2 * 16384;  // per K-block: h hi rows, then h lo rows
   static constexpr int kRawBytes = 8192;
   static constexpr int kRaw = kRawBytes;
   static constexpr int kJobScales = 128 * (kInter / 16);  // a job's 128 scale rows of 40 B, loaded once per job
-  static constexpr uint32_t kASlot = 64;        // per K-block 32 columns
+  static constexpr uint32_t kASlot = 32 * kStageKB;  // per K-block 32 columns
 };
 // Stages: activation tiles in shared memory and A slots in TMEM, two K-blocks each.
-constexpr int kPfKStages = 2;
-constexpr int kPfStageKB = 2;
 // TMEM: columns [0, 256) hold the accumulators as two halves of 128 columns.
 // Down jobs always take one half (a tile of <= 64 pairs: N = hi rows + lo
 // rows of the box; larger tiles: hi and lo MMAs into the same N = 128
@@ -258,11 +267,11 @@ template <int MODE>
 struct PfSmem {
   using C = PfCfg<MODE>;
   static constexpr int kB = 0;
-  static constexpr int kRaw = kB + kPfKStages * C::kBMax;
+  static constexpr int kRaw = kB + C::kKStages * C::kBMax;
   static constexpr int kJs = kRaw + C::kRStages * C::kRaw;  // down: two per-job scale buffers
   static constexpr int kBar = kJs + 2 * C::kJobScales;
-  static constexpr int kCols = kBar + 512;     // per-column epilogue data: 2 x 3 x 128 words
-  static constexpr int kTotal = kCols + 2 * 3 * 128 * 4 + 1024;  // + alignment slack
+  static constexpr int kCols = kBar + 512;     // per-column epilogue data: 2 x 2 x 128 words
+  static constexpr int kTotal = kCols + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
 };
 
 // Activation tensor maps with boxes of 16, 32, 64 and 128 rows (a job loads
@@ -324,40 +333,40 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     pf_gemm_kernel(const __grid_constant__ PfMaps maps, const PfArgs args) {
   using C = PfCfg<MODE>;
   using L = PfSmem<MODE>;
-  constexpr int KS = kPfKStages, SK = kPfStageKB, RS = C::kRStages, KB = C::kKBlocks, NST = KB / SK;
+  constexpr int KS = C::kKStages, SK = C::kStageKB, RS = C::kRStages, KB = C::kKBlocks, NST = KB / SK;
   constexpr int NI = MODE == kGateUp ? 2 : 1;  // MMA issuers (gate/up: one for the gate rows, one for the up rows)
   static_assert(KB % SK == 0 && C::kRawKB % SK == 0 || SK % C::kRawKB == 0, "stage / raw stage sizes");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   // stage s: activation tile s in shared memory + A slot s in TMEM.
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 16 dequant warps
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 8 dequant warps
   uint64_t* k_empty = k_full + KS;   // NI MMA issuers (commit)
   uint64_t* r_full = k_empty + KS;
-  uint64_t* r_empty = r_full + RS;   // 16 dequant warps
+  uint64_t* r_empty = r_full + RS;   // 8 dequant warps
   uint64_t* tm_full = r_empty + RS;  // [2] accumulator halves: NI MMA issuers -> epilogue
   uint64_t* tm_empty = tm_full + 2;  // [2] 4 epilogue warps
   uint64_t* js_full = tm_empty + 2;  // [2] down: per-job scale rows
-  uint64_t* js_empty = js_full + 2;  // [2] 16 dequant warps
+  uint64_t* js_empty = js_full + 2;  // [2] 8 dequant warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(js_empty + 2);
   volatile uint32_t* abort = tslot + 1;
-  int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][3][128]: token, weight bits, exponent
+  int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][2][128]: per-column factors (epilogue)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     *abort = 0u;
     for (int s = 0; s < KS; ++s) {
-      mbar_init(&k_full[s], 17);
+      mbar_init(&k_full[s], 9);
       mbar_init(&k_empty[s], NI);
     }
     for (int s = 0; s < RS; ++s) {
       mbar_init(&r_full[s], 1);
-      mbar_init(&r_empty[s], 16);
+      mbar_init(&r_empty[s], 8);
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&tm_full[h], NI);
       mbar_init(&tm_empty[h], 4);
       mbar_init(&js_full[h], 1);
-      mbar_init(&js_empty[h], 16);
+      mbar_init(&js_empty[h], 8);
     }
     fence_mbar_init();
   }
@@ -507,15 +516,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       hv.done(h);
     }
-  } else if (warp >= 4 && warp < 20) {
+  } else if (warp >= 4 && warp < 12) {
     // ---------------- dequantisers: warp 4 + w writes TMEM lanes 32 (w % 4) ..
-    // + 31 of the A slot, one K-block (j = w / 8) of the stage.  Gate/up:
-    // matrix i = (w / 4) % 2 (gate / up rows of the job's 128 features), 64 k;
-    // down: K half i = (w / 4) % 2 (32 k) of the job's 128 output rows.  A
-    // warp converts its K-block into registers before it waits for the A slot,
-    // so the conversion overlaps the MMAs of the previous stage.
+    // + 31 of the A slot, both K-blocks of the stage.  Gate/up: matrix
+    // i = w / 4 (gate / up rows of the job's 128 features), 64 k per K-block;
+    // down: K half i = w / 4 (32 k) of the job's 128 output rows.  A warp
+    // converts the stage into registers before it waits for the A slot, so
+    // the conversion overlaps the MMAs of the previous stage.
     const int w = warp - 4;
-    const int i = (w >> 2) & 1, j = w >> 3;
+    const int i = w >> 2;
     const int r = 32 * (w & 3) + lane;    // A row = TMEM lane
     const int d = 128 * i + r;            // gate/up: row of the raw stage ([gate|up][128])
     // raw row of this thread in a raw stage (gate/up: 128-byte rows, 128-byte
@@ -523,7 +532,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int raw_row = MODE == kGateUp ? d * 128 : r * 64;
     const int swz = MODE == kGateUp ? (d & 7) : ((r >> 1) & 3);
     const uint32_t lane_base = static_cast<uint32_t>(32 * (w & 3)) << 16;
-    const uint32_t acol = (MODE == kGateUp ? 64u * j + 32u * i : 32u * j + 16u * i) + lane_base;
+    constexpr int NV = MODE == kGateUp ? 32 : 16;  // f16x2 words per K-block and thread
     int st = 0, jj = 0;
     uint4 sc = make_uint4(0, 0, 0, 0);
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
@@ -531,57 +540,62 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
       for (int q = 0; q < NST; ++q, ++st) {
         const int s = st % KS;
-        const int kb = SK * q + j;
-        const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
-        const int rt = gkb / C::kRawKB, sr = rt % RS;
-        const int kr = kb % C::kRawKB;  // K-block within the raw stage
-        const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
-        if (kr < SK) {  // this warp's first K-block of the raw stage
-          pf_wait(&r_full[sr], (rt / RS) & 1, abort);
-          if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
-        }
-        const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
-                                            : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
-        const uint8_t* raw = stage + raw_row;
-        uint32_t sa0, sa1, sa2, sa3;
-        e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
-        e4m3x2_to_bcast(sw >> 16, sa2, sa3);
-        constexpr int NV = MODE == kGateUp ? 32 : 16;
-        uint32_t v[NV];
-        if (MODE == kGateUp) {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
-          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
-          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t v[SK][NV];
 #pragma unroll
-          for (int jq = 0; jq < 8; ++jq) {
-            uint32_t hf[4];
-            e2m1x8_to_f16x2(words[jq], hf);
-            const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[(4 * jq + e) % NV] = hmul2_u32(hf[e], sc2);
+        for (int j = 0; j < SK; ++j) {
+          const int kb = SK * q + j;
+          const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
+          const int rt = gkb / C::kRawKB, sr = rt % RS;
+          const int kr = kb % C::kRawKB;  // K-block within the raw stage
+          const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
+          if (kr == 0) {
+            pf_wait(&r_full[sr], (rt / RS) & 1, abort);
+            if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
           }
-        } else {
-          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
-          const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
-          const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
+          const uint32_t sw = MODE == kGateUp ? (kr == 0 ? sc.x : (kr == 1 ? sc.y : (kr == 2 ? sc.z : sc.w)))
+                                              : *reinterpret_cast<const uint32_t*>(jsc + 4 * kb);
+          const uint8_t* raw = stage + raw_row;
+          uint32_t sa0, sa1, sa2, sa3;
+          e4m3x2_to_bcast(sw & 0xffffu, sa0, sa1);
+          e4m3x2_to_bcast(sw >> 16, sa2, sa3);
+          if (MODE == kGateUp) {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr) ^ swz) << 4));
+            const uint4 w1 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + 1) ^ swz) << 4));
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int jq = 0; jq < 4; ++jq) {
-            uint32_t hf[4];
-            e2m1x8_to_f16x2(words[jq], hf);
-            const uint32_t sc2 = jq < 2 ? s0 : s1;
+            for (int jq = 0; jq < 8; ++jq) {
+              uint32_t hf[4];
+              e2m1x8_to_f16x2(words[jq], hf);
+              const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[4 * jq + e] = hmul2_u32(hf[e], sc2);
+              for (int e = 0; e < 4; ++e) v[j][(4 * jq + e) % NV] = hmul2_u32(hf[e], sc2);
+            }
+          } else {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
+            const uint32_t words[4] = {w0.x, w0.y, w0.z, w0.w};
+            const uint32_t s0 = i ? sa2 : sa0, s1 = i ? sa3 : sa1;
+#pragma unroll
+            for (int jq = 0; jq < 4; ++jq) {
+              uint32_t hf[4];
+              e2m1x8_to_f16x2(words[jq], hf);
+              const uint32_t sc2 = jq < 2 ? s0 : s1;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) v[j][4 * jq + e] = hmul2_u32(hf[e], sc2);
+            }
           }
-        }
-        if (kr >= C::kRawKB - SK) {  // this warp's last K-block of the raw stage: release it
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&r_empty[sr]);
+          if (kr == C::kRawKB - 1) {  // last K-block of the raw stage: release it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[sr]);
+          }
         }
         pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
         tc_fence_after();
-        const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + acol;
-        if (MODE == kGateUp) tmem_st_x32(aslot, *reinterpret_cast<uint32_t(*)[32]>(v));
-        else tmem_st_x16(aslot, *reinterpret_cast<uint32_t(*)[16]>(v));
+        const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + lane_base;
+#pragma unroll
+        for (int j = 0; j < SK; ++j) {
+          if (MODE == kGateUp) tmem_st_x32(aslot + 64 * j + 32 * i, *reinterpret_cast<uint32_t(*)[32]>(v[j]));
+          else tmem_st_x16(aslot + 32 * j + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(v[j]));
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -591,20 +605,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
     }
-  } else if (warp >= 20) {
-    // ---------------- epilogue: warp 20 + q reads TMEM lanes 32q .. 32q + 31
-    const int q = warp - 20;
-    const int et = threadIdx.x - 640;  // 0..127
+  } else if (warp >= 12) {
+    // ---------------- epilogue: warp 12 + q reads TMEM lanes 32q .. 32q + 31
+    const int q = warp - 12;
+    const int et = threadIdx.x - 384;  // 0..127
     int jj = 0;
     PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
       const int t = u / C::kSub, sub = u % C::kSub;
       const int e = args.tile_e[t], p0 = args.tile_p0[t], n = args.tile_n[t];
-      int* ccol = cols + (jj & 1) * 3 * 128;
+      // per-column factors of the job: gate/up: ws2_g 2^-ex, ws2_u 2^-ex;
+      // down: coef ws2_d 2^-eh and the token's output row offset
+      float* cf = reinterpret_cast<float*>(cols) + (jj & 1) * 2 * 128;
+      int* ci = reinterpret_cast<int*>(cf + 128);
       if (et < n) {
-        ccol[et] = args.pair_tok[p0 + et];
-        ccol[128 + et] = __float_as_int(args.pair_w[p0 + et]);
-        ccol[256 + et] = args.pair_ex[p0 + et];
+        const int ex = args.pair_ex[p0 + et];
+        if (MODE == kGateUp) {
+          cf[et] = pow2_mul(args.s2l[3 * e + 0], -ex);
+          reinterpret_cast<float*>(ci)[et] = pow2_mul(args.s2l[3 * e + 1], -ex);
+        } else {
+          cf[et] = pow2_mul(args.pair_w[p0 + et] * args.s2l[3 * e + 2], -ex);
+          ci[et] = args.pair_tok[p0 + et];
+        }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       const int h = hv.pick(n);
@@ -614,38 +636,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const uint32_t t0 = tmem + (static_cast<uint32_t>(32 * q) << 16) + (h == 1 ? 128u : 0u);
       if (MODE == kGateUp) {
         const uint32_t t1 = t0 + (h == 2 ? 128u : 64u);
-        const float ws_g = args.s2l[3 * e + 0], ws_u = args.s2l[3 * e + 1];
-        float* hrow = args.h32 + 128 * sub + 32 * q + lane;
+        const float* fu = reinterpret_cast<const float*>(ci);
+        float* hrow = args.h32 + static_cast<int64_t>(p0) * kInter + 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 16) {
           uint32_t vg[16], vu[16];
           tmem_ld_x16(t0 + c0, vg);
           tmem_ld_x16(t1 + c0, vu);
+          const int lim = n - c0;
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const int col = c0 + c;
-            if (col < n) {
-              const int ex = ccol[256 + col];
-              const float gg = pow2_mul(__uint_as_float(vg[c]), -ex) * ws_g;
-              const float uu = pow2_mul(__uint_as_float(vu[c]), -ex) * ws_u;
-              hrow[static_cast<int64_t>(p0 + col) * kInter] = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
+            if (c < lim) {
+              const float gg = __uint_as_float(vg[c]) * cf[c0 + c];
+              const float uu = __uint_as_float(vu[c]) * fu[c0 + c];
+              hrow[(c0 + c) * kInter] = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
             }
           }
         }
       } else {
-        const float ws_d = args.s2l[3 * e + 2];
         const int rows = 16 << pf_box(n);
-        const int row = 128 * sub + 32 * q + lane;
+        float* orow = args.out + 128 * sub + 32 * q + lane;
         for (int c0 = 0; c0 < n; c0 += 16) {
           uint32_t vh[16], vl[16];
           tmem_ld_x16(t0 + c0, vh);
           if (rows < 128) tmem_ld_x16(t0 + rows + c0, vl);  // lo columns (128-row boxes: summed by the MMA)
+          const int lim = n - c0;
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const int col = c0 + c;
-            if (col < n) {
-              const float f = pow2_mul(__int_as_float(ccol[128 + col]) * ws_d, -ccol[256 + col]);
+            if (c < lim) {
               const float v = rows < 128 ? __uint_as_float(vh[c]) + __uint_as_float(vl[c]) : __uint_as_float(vh[c]);
-              atomicAdd(args.out + static_cast<int64_t>(ccol[col]) * kHid + row, v * f);
+              atomicAdd(orow + static_cast<int64_t>(ci[c0 + c]) * kHid, v * cf[c0 + c]);
             }
           }
         }
