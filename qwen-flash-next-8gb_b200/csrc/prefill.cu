@@ -418,23 +418,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == 3) {
     // ---------------- weight producer (warp 3; one elected lane issues): per raw stage the job's raw rows of
     // kRawKB K-blocks (gate/up: with their scale bytes); per down job its
-    // 128 scale rows.  At the start of each job the next job's raw rows are
-    // prefetched into L2.
-    auto prefetch_job = [&](int ux) {
-      if (ux >= n_jobs) return;
-      const int tx = ux / C::kSub, subx = ux % C::kSub;
-      const uint8_t* blkp = args.table + (args.base + args.tile_e[tx]) * kBlock;
-      if (MODE == kGateUp) {
-        bulk_prefetch_l2(blkp + kOGW + 128 * subx * (kHid / 2), 128 * (kHid / 2));
-        bulk_prefetch_l2(blkp + kOUW + 128 * subx * (kHid / 2), 128 * (kHid / 2));
-      } else {
-        bulk_prefetch_l2(blkp + kODW + 128 * subx * (kInter / 2), 128 * (kInter / 2));
-      }
-    };
-    if (elect_one()) prefetch_job(blockIdx.x);
+    // 128 scale rows.  (An L2 prefetch of the next job's rows measured
+    // slower: with the activation rows it overflows L2 and doubles DRAM reads.)
     int rt = 0, jj = 0;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
-      if (elect_one()) prefetch_job(u + gridDim.x);
       const int t = u / C::kSub, sub = u % C::kSub;
       const int blk = static_cast<int>(args.base + args.tile_e[t]);
       if (MODE == kDown) {  // the job's scale rows: [64 row pairs][80 B]
