@@ -55,6 +55,8 @@ def parse():
                    help="decode: config 2 (default, the headline line); prefill: config 3")
     p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
     p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
+    p.add_argument("--variant", type=int, default=0,
+                   help="decode kernel path: 0 auto (slice path for K <= 10), 3 stream, 4 slice, 2 CUDA-core")
     return p.parse_args()
 
 
@@ -395,7 +397,10 @@ def main():
 
     def step_eager(r, outs=None):
         for l in range(L):
-            y = qmoe.moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], x[r, l], hb, ob)
+            if args.variant:
+                y = qmoe._moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], x[r, l], hb, args.variant)
+            else:
+                y = qmoe.moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], x[r, l], hb, ob)
             if outs is not None:
                 outs.append(y)
 
@@ -486,7 +491,9 @@ def main():
                 "steps": E, "ms_per_step": ms_e2e / E, "path": "qmoe.moe_decode (eager, public API)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "kernel": "moe_decode_stream (one launch per decode layer)",
+                     "kernel": {0: "moe_decode_slice", 4: "moe_decode_slice", 3: "moe_decode_stream",
+                                2: "moe_gate_up_generic + moe_down_generic", 1: "moe_decode_persistent"}
+                     .get(args.variant, "?") + " (one launch per decode layer)",
                      "traffic": None, "per_launch_bytes": LAYER_BYTES},
         "gpu_launches": args.steps * L,
         "clocks": clk.summary(),

@@ -102,11 +102,16 @@ int qfn_block_deq(const uint8_t* blk, const float s2[3], float* gate, float* up,
  *           it holds h, as in the reference.
  *   out:    f32[2560] device; written (not accumulated).
  *   1 <= K <= QFN_MAX_TOPK.
- *   K <= 10 runs the stream path (one cooperative launch per layer: the
- *   whole layer requested from HBM at entry, mma.sync dot products, a grid
- *   barrier between h and the down projection); larger K runs the two-launch
- *   CUDA-core path.  Results are bit-identical between calls with the same
- *   inputs (fixed reduction order).
+ *   K <= 10 on a 148-SM part with a 16-byte aligned out runs the slice path:
+ *   one cooperative launch per layer without a grid-wide barrier (every CTA
+ *   owns one expert's 32-48 features, computes their h on chip and
+ *   multiplies them into the matching column slice of the down rows; the
+ *   CTAs' partial outputs meet in out through fp32 atomic adds, so repeated
+ *   calls agree to fp32 rounding of the summation order, not bit for bit).
+ *   The library keeps a small per-device array of call counters for it
+ *   (file-scope device memory, nothing allocated per call).  Otherwise K <=
+ *   10 runs the stream path (bit-reproducible; a grid barrier between h and
+ *   the down projection) and larger K the two-launch CUDA-core path.
  */
 int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                    const float* s2, const float* coef, const void* x, int x_dtype,
@@ -115,11 +120,11 @@ int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
 /*
  * qfn_moe_decode_variant -- qfn_moe_decode with the kernel path chosen by the
  * caller (no counterpart in the reference; for tests and measurements):
- * variant 0 = automatic (stream path for K <= 10, else CUDA-core path),
+ * variant 0 = automatic (slice path for K <= 10, else CUDA-core path),
  * 1 = tensor-core path (one cooperative persistent launch: tcgen05
  * block-scaled FP4 MMA for gate/up, mma.sync for down; K <= 10; weight block
  * scales must be positive), 2 = CUDA-core path (two launches), 3 = stream path
- * (K <= 10).
+ * (K <= 10, bit-reproducible), 4 = slice path (K <= 10, out 16-byte aligned).
  */
 int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                            const float* s2, const float* coef, const void* x, int x_dtype,

@@ -203,7 +203,7 @@ int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, u
 namespace {
 struct TmapNdEntry {
   const void* base;
-  int dtype, device, rank, swizzle;
+  int dtype, device, rank, swizzle, promotion;
   uint64_t dims[5], strides[4];
   uint32_t box[5];
   CUtensorMap map;
@@ -217,13 +217,13 @@ namespace qfn {
 
 int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
                   const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out,
-                  CUtensorMapSwizzle swizzle) {
+                  CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promotion) {
   if (rank < 1 || rank > 5) return set_error(QFN_ERR_INVALID_ARG, "tensor map rank %d", rank);
   std::lock_guard<std::mutex> lk(g_tmap_mu);
   for (int i = 0; i < g_tmapnd_count; ++i) {
     const TmapNdEntry& t = g_tmapsnd[i];
     if (t.base != base || t.dtype != static_cast<int>(dtype) || t.device != device || t.rank != rank ||
-        t.swizzle != static_cast<int>(swizzle))
+        t.swizzle != static_cast<int>(swizzle) || t.promotion != static_cast<int>(promotion))
       continue;
     bool same = true;
     for (int d = 0; d < rank; ++d) same = same && t.dims[d] == dims[d] && t.box[d] == box[d];
@@ -250,7 +250,7 @@ int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const u
   }
   for (int d = 0; d + 1 < rank; ++d) s64[d] = strides[d];
   CUresult r = g_encode(&m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d64, s64, b32, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promotion,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled (%d-D) failed (%d)", rank, static_cast<int>(r));
   TmapNdEntry& t = g_tmapsnd[g_tmapnd_count < kTmapNdSlots ? g_tmapnd_count++ : (g_tmapnd_next++ % kTmapNdSlots)];
@@ -259,6 +259,7 @@ int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const u
   t.device = device;
   t.rank = rank;
   t.swizzle = static_cast<int>(swizzle);
+  t.promotion = static_cast<int>(promotion);
   for (int d = 0; d < rank; ++d) {
     t.dims[d] = dims[d];
     t.box[d] = box[d];

@@ -16,6 +16,7 @@
 //    were complete before gate_up started), then wait for gate_up's h.
 #include <cooperative_groups.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -1155,12 +1156,26 @@ static int launch_moe_decode_stream(const uint8_t* table, int64_t n_blocks, cons
   return check_launch("moe_decode_stream");
 }
 
+}  // namespace qfn
+
+#include "decode_slice.cuh"
+
+namespace qfn {
+
 static int launch_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
                              const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
                              cudaStream_t st, int variant) {
   DeviceInfo* dev;
   int rc = current_device(&dev);
   if (rc) return rc;
+  if (variant == 0 || variant == 4) {
+    // The slice path adds 16-byte vectors into out.
+    if (slice_fits(K, dev) && aligned(out, 16))
+      return launch_moe_decode_slice(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, st, dev);
+    if (variant == 4)
+      return set_error(QFN_ERR_UNSUPPORTED,
+                       "slice decode path needs K <= 10, a 148-SM-class device and a 16-byte aligned out");
+  }
   if (variant == 1) {
     // The persistent path keeps a CTA's whole share of the layer in shared memory.
     if (!persistent_fits(K, dev))
@@ -1210,11 +1225,12 @@ extern "C" int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, co
                                       int K, int variant, qfn_stream_t stream) {
   int rc = check_decode_args(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K);
   if (rc) return rc;
-  QFN_REQUIRE(variant >= 0 && variant <= 3, QFN_ERR_INVALID_ARG, "qfn_moe_decode_variant: variant %d", variant);
+  QFN_REQUIRE(variant >= 0 && variant <= 4, QFN_ERR_INVALID_ARG, "qfn_moe_decode_variant: variant %d", variant);
   QFN_REQUIRE(variant != 1 || K <= kFastMaxK, QFN_ERR_UNSUPPORTED,
               "qfn_moe_decode_variant: the tensor-core path takes K <= %d", kFastMaxK);
   QFN_REQUIRE(variant != 3 || K <= kSMaxK, QFN_ERR_UNSUPPORTED,
               "qfn_moe_decode_variant: the stream path takes K <= %d", kSMaxK);
+  QFN_REQUIRE(variant != 4 || K <= 10, QFN_ERR_UNSUPPORTED, "qfn_moe_decode_variant: the slice path takes K <= 10");
   return launch_moe_decode(table, n_blocks, sidx, s2, coef, x, x_dtype, h_buf, out, K, as_stream(stream), variant);
 }
 

@@ -60,6 +60,7 @@ int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, u
 // dimension i + 1.
 int tensor_map_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
                   const uint64_t* strides, const uint32_t* box, int device, CUtensorMap* out,
-                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CUtensorMapL2promotion promotion = CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
 
 }  // namespace qfn

@@ -66,7 +66,8 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     odd = ctypes.c_void_p(0x10001)
     assert lib.qfn_moe_decode(odd, 1, fake, fake, fake, fake, 1, fake, fake, 10, None) == 2
     # variant selection
-    assert lib.qfn_moe_decode_variant(fake, 1, fake, fake, fake, fake, 1, fake, fake, 10, 4, None) == 1
+    assert lib.qfn_moe_decode_variant(fake, 1, fake, fake, fake, fake, 1, fake, fake, 10, 5, None) == 1
+    assert lib.qfn_moe_decode_variant(fake, 1, fake, fake, fake, fake, 1, fake, fake, 11, 4, None) == 4
     assert lib.qfn_moe_decode_variant(fake, 1, fake, fake, fake, fake, 1, fake, fake, 11, 3, None) == 4
     assert lib.qfn_moe_decode_variant(fake, 1, fake, fake, fake, fake, 1, fake, fake, 11, 1, None) == 4
     assert lib.qfn_device_status(None, 0) == 1

@@ -62,8 +62,11 @@ def test_block_deq_bit_exact(golden):
 
 
 # ---------------------------------------------------------------- decode expert layer
-VARIANTS = [qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_CUDA_CORE, qmoe.VARIANT_STREAM]
-SMALL_K_VARIANTS = (qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_STREAM)   # K <= 10
+VARIANTS = [qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_CUDA_CORE, qmoe.VARIANT_STREAM, qmoe.VARIANT_SLICE]
+SMALL_K_VARIANTS = (qmoe.VARIANT_TENSOR_CORE, qmoe.VARIANT_STREAM, qmoe.VARIANT_SLICE)   # K <= 10
+# The slice path (the default for K <= 10) sums its per-CTA partials with fp32
+# atomics: repeated calls agree to fp32 rounding of the summation order.
+REPEAT_GRADE = 1e-5
 
 
 def run_decode(table, sidx, s2, coef, x, variant=qmoe.VARIANT_AUTO):
@@ -139,7 +142,10 @@ def test_moe_decode_repeated_calls_identical(table24, variant):
             synthetic.make_x(2560, 11))
     a, _ = run_decode(table, *args, variant=variant)
     b, _ = run_decode(table, *args, variant=variant)
-    assert np.array_equal(a, b)      # fixed reduction order: bit-reproducible
+    if variant == qmoe.VARIANT_SLICE:
+        assert rel_err(a, b) <= REPEAT_GRADE and np.argmax(a) == np.argmax(b)
+    else:
+        assert np.array_equal(a, b)      # fixed reduction order: bit-reproducible
 
 
 def test_moe_decode_paths_agree(table24):
@@ -185,7 +191,8 @@ def test_moe_decode_graph_capture(table24):
     g.replay()
     torch.cuda.synchronize()
     want = qmoe.moe_decode(table, sidx, s2, coef, x, hb, ob)
-    assert torch.equal(y, want) and not torch.equal(y, eager)
+    assert rel_err(y.cpu().numpy(), want.cpu().numpy()) <= REPEAT_GRADE
+    assert rel_err(y.cpu().numpy(), eager.cpu().numpy()) > 1e-2
 
 
 # ---------------------------------------------------------------- FP8 GEMV
