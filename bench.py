@@ -51,8 +51,10 @@ def parse():
     p.add_argument("--cpu-layers", type=int, default=4, help="layers timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                   help="decode: config 2 (default, the headline line); prefill: config 3")
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "gemv", "batch-decode"],
+                   help="decode: config 2 (default, the headline line); prefill: config 3; gemv: config 1; "
+                        "batch-decode: config 4")
+    p.add_argument("--batch", type=int, default=64, help="batch-decode: tokens per GPU per step (config 4: 64)")
     p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
     p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
     p.add_argument("--variant", type=int, default=0,
@@ -133,6 +135,26 @@ def run_reference(args, rank):
     import oracle
     import synthetic
     cores = oracle.threads(os.cpu_count())
+    if args.workload == "gemv":
+        N, K = GEMV_SHAPES[0]
+        q, sc = oracle.to_fp8_rows(synthetic.gemv_weights(N, K, seed=args.seed).float().numpy())
+        x = synthetic.make_x(K, seed=args.seed).float().numpy()
+        for _ in range(args.warmup):
+            oracle.gemv(q, sc, x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            oracle.gemv(q, sc, x)
+        dt = time.perf_counter() - t0
+        v = args.steps * gemv_bytes(N, K) / dt / 1e9
+        sample = f"one {N}x{K} GEMV per step, C oracle, {cores} OpenMP threads"
+        print(json.dumps({
+            "impl": "reference", "metric": GEMV_METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"fp8-gemv (config 1): {N}x{K} per call, bs=1", "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
     blocks = synthetic.make_blocks(TOPK, seed=args.seed)
     sidx = np.arange(TOPK, dtype=np.int32)
     s2 = synthetic.make_s2(TOPK)
@@ -370,6 +392,329 @@ def prefill_cpu_baseline(args, table, s2, x, ti, tv):
                       f"{dt:.1f} s"}
 
 
+# ---------------------------------------------------------------- FP8 GEMV (config 1)
+GEMV_SHAPES = ((12288, 2560), (2560, 4096))   # the DeltaNet projections of config 1 (N x K)
+GEMV_COPIES = 8                                # weight copies rotated per shape (8 x 31.5 MB > 2 x L2)
+GEMV_CALLS = 64                                # calls per graph replay (one step)
+GEMV_METRIC = "FP8 E4M3 row-scaled GEMV HBM GB/s (12288x2560, bs=1, per call)"
+
+
+def gemv_bytes(N, K):
+    return N * K + 4 * N + 2 * K + 2 * N       # weights + row scales + x (bf16) + y (bf16)
+
+
+def run_gemv(args, rank, world):
+    import torch
+    import fp8gemv
+    import synthetic
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 11)
+    per_shape = {}
+    for (N, K) in GEMV_SHAPES:
+        qs, ss = [], []
+        for _ in range(GEMV_COPIES):
+            w = torch.randn(N, K, device=dev, generator=g) * 0.02        # W ~ N(0, 0.02) (config 1)
+            q, sc = synthetic.to_fp8_rows(w)                              # the engine's quantizer
+            qs.append(q.contiguous())
+            ss.append(sc.view(-1).contiguous())
+            del w
+        xs = [torch.randn(K, device=dev, generator=g).to(torch.bfloat16) for _ in range(4)]
+        per_shape[(N, K)] = (qs, ss, xs)
+
+    def calls(N, K):
+        qs, ss, xs = per_shape[(N, K)]
+        for i in range(GEMV_CALLS):
+            fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], xs[i % 4])
+
+    graphs = {}
+    for shape in GEMV_SHAPES:
+        calls(*shape)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            calls(*shape)
+        graphs[shape] = gr
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    us_call = {}
+    clk_summary = None
+    for shape in GEMV_SHAPES:
+        for _ in range(max(args.warmup, 3)):
+            graphs[shape].replay()
+        barrier()
+        with ClockSampler(local) as clk:
+            e0.record(st)
+            for _ in range(args.steps):
+                graphs[shape].replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist is not None:
+            t_ = torch.tensor([ms], device=dev)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            ms = float(t_.item())
+        us_call[shape] = ms * 1e3 / (args.steps * GEMV_CALLS)
+        if shape == GEMV_SHAPES[0]:
+            clk_summary = clk.summary()
+            ms_main = ms
+    N0, K0 = GEMV_SHAPES[0]
+    b0 = gemv_bytes(N0, K0)
+    value = world * b0 / (us_call[GEMV_SHAPES[0]] * 1e-6) / 1e9
+
+    # e2e: the public API per call, x copied in from pinned host memory, y copied back
+    qs, ss, xs = per_shape[GEMV_SHAPES[0]]
+    h_x = [x.cpu().pin_memory() for x in xs]
+    h_y = torch.empty(N0, dtype=torch.bfloat16).pin_memory()
+    d_x = torch.empty_like(xs[0])
+    E = 256
+
+    def e2e_call(i):
+        d_x.copy_(h_x[i % 4], non_blocking=True)
+        y = fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], d_x)
+        h_y.copy_(y, non_blocking=True)
+
+    for i in range(8):
+        e2e_call(i)
+    barrier()
+    e0.record(st)
+    for i in range(E):
+        e2e_call(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1)
+    if dist is not None:
+        t_ = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t_.item())
+    e2e_value = world * E * b0 / (ms_e2e * 1e-3) / 1e9
+
+    peak, peak_kind = peaks()
+    achieved = b0 / (us_call[GEMV_SHAPES[0]] * 1e-6) / 1e9
+    line = {
+        "metric": GEMV_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_main / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 weights, bf16 x, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"fp8-gemv (config 1): {N0}x{K0} per call, bs=1; a step = {GEMV_CALLS} calls in one "
+                               f"CUDA graph over {GEMV_COPIES} rotated weight copies",
+                   "us_per_call": {f"{N}x{K}": us_call[(N, K)] for (N, K) in GEMV_SHAPES},
+                   "gbs_per_shape": {f"{N}x{K}": gemv_bytes(N, K) / (us_call[(N, K)] * 1e-6) / 1e9
+                                     for (N, K) in GEMV_SHAPES},
+                   "bytes_per_call": {f"{N}x{K}": gemv_bytes(N, K) for (N, K) in GEMV_SHAPES},
+                   "l2": f"no flush: {GEMV_COPIES} rotated weight copies per shape "
+                         f"({GEMV_COPIES * N0 * K0 / 1e6:.0f} MB > 2 x 126 MB L2)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": K0 * 2, "d2h_bytes_per_step": N0 * 2,
+                "steps": E, "us_per_call": ms_e2e * 1e3 / E,
+                "path": "fp8gemv.gemv (public API, eager) with x from pinned host memory and y copied back"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "kernel": "gemv_stream_kernel", "traffic": None,
+                     "per_launch_bytes": b0},
+        "gpu_launches": args.steps * GEMV_CALLS,
+        "clocks": clk_summary,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle
+        cores = oracle.threads(os.cpu_count())
+        q = qs[0].view(torch.uint8).cpu().numpy()
+        sc = ss[0].cpu().numpy()
+        xf = xs[0].float().cpu().numpy()
+        oracle.gemv(q, sc, xf)
+        n = 3
+        t0 = time.perf_counter()
+        for _ in range(n):
+            oracle.gemv(q, sc, xf)
+        dt = (time.perf_counter() - t0) / n
+        line["cpu_baseline"] = {"value": b0 / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} calls of the {N0}x{K0} GEMV (C oracle: e4m3 decode, fp64 dot "
+                                          f"products), {dt * 1e3:.1f} ms/call"}
+    if dist is not None:
+        del graphs
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+# ---------------------------------------------------------------- batched decode (config 4)
+BD_METRIC = "batched-decode tokens/s (batch 64 per GPU, 48-layer NVFP4 MoE stack, top-10 of 512 uniform)"
+
+
+def run_batch_decode(args, rank, world):
+    """Config 4: a step = one decode step of `--batch` tokens per GPU through all
+    `--n-layers` MoE layers; router logits ~ N(0,1) (uniform popularity), top-10
+    of 512 per layer, x ~ N(0,1) bf16 per layer.  1 GPU: the grouped expert GEMM
+    (qmoe.moe_prefill) per layer on the full table, one CUDA graph per step.
+    N GPUs: expert-parallel (each rank holds 512/N experts of every layer, its
+    own --batch tokens; NCCL all-to-all dispatch and combine per layer)."""
+    import torch
+    import qmoe
+    import routing
+    from expert_table import ExpertTable
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = shard = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        import ep
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        shard = ep.ExpertShard(N_EXPERTS, world, rank)
+    L, B = args.n_layers, args.batch
+    e_local = N_EXPERTS // world
+    table = ExpertTable(K=TOPK, dev=dev, n_layers=L, n_experts=e_local)
+    table.fill_synthetic(seed=args.seed + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 23 + 1000 * rank)
+    R = 2
+    xs = torch.randn(R, L, B, HID, device=dev, generator=g).to(torch.bfloat16)
+    ti, tv = routing.route(torch.randn(R * L * B, N_EXPERTS, device=dev, generator=g), TOPK)
+    ti, tv = ti.view(R, L, B, TOPK).contiguous(), tv.view(R, L, B, TOPK).contiguous()
+    distinct = [[int(torch.unique(ti[r, l]).numel()) for l in range(L)] for r in range(R)]
+
+    def layer(x, t, v, l):
+        if shard is None:
+            return qmoe.moe_prefill(x, t, v, table.slots, table.s2[l], l)
+        return ep.moe_prefill_ep(x, t, v, table.slots, table.s2[l], l, shard)
+
+    def step(r):
+        for l in range(L):
+            layer(xs[r, l], ti[r, l], tv[r, l], l)
+
+    graphs = None
+    if shard is None:  # the exchange syncs on the host for its split sizes: EP runs eagerly
+        step(0)
+        torch.cuda.synchronize()
+        graphs = []
+        for r in range(R):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(r)
+            graphs.append(gr)
+
+    def run(r):
+        if graphs is not None:
+            graphs[r % R].replay()
+        else:
+            step(r % R)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(max(args.warmup, 3)):
+        run(i)
+    barrier()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(st)
+        for i in range(args.steps):
+            run(i)
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist is not None:
+        t_ = torch.tensor([ms], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms = float(t_.item())
+    tok_s = world * B / (ms * 1e-3)
+    step_bytes = sum(sum(d) * BLOCK for d in distinct) / R + L * B * HID * (2 + 4)   # experts + x in + fp32 out
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+
+    # e2e: per step every layer's x, ti, tv from pinned host memory and its fp32 output back
+    h_x, h_ti, h_tv = xs[0].cpu().pin_memory(), ti[0].cpu().pin_memory(), tv[0].cpu().pin_memory()
+    h_out = torch.empty(L, B, HID, dtype=torch.float32).pin_memory()
+    d_x, d_ti, d_tv = torch.empty_like(xs[0]), torch.empty_like(ti[0]), torch.empty_like(tv[0])
+    h2d = d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2
+    d2h = L * B * HID * 4
+
+    def e2e_step():
+        d_x.copy_(h_x, non_blocking=True)
+        d_ti.copy_(h_ti, non_blocking=True)
+        d_tv.copy_(h_tv, non_blocking=True)
+        for l in range(L):
+            h_out[l].copy_(layer(d_x[l], d_ti[l], d_tv[l], l), non_blocking=True)
+
+    E = min(args.e2e_steps, 8)
+    e2e_step()
+    barrier()
+    e0.record(st)
+    for _ in range(E):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / E
+    if dist is not None:
+        t_ = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t_.item())
+
+    peak, peak_kind = peaks()
+    line = {
+        "metric": BD_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, "
+                                      "fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"batch-decode (config 4): {B} tokens per GPU, {L} layers, top-{TOPK} of "
+                               f"{N_EXPERTS} uniform; {sum(map(sum, distinct)) / R / L:.0f} distinct experts per "
+                               f"layer per rank's tokens",
+                   "hbm_gbs": gbs, "bytes_per_step": step_bytes,
+                   "l2": "no flush: each step reads ~48 GB of distinct expert blocks (>> 126 MB L2)",
+                   "parallelism": f"expert-parallel x{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                   else "single GPU"},
+        "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
+                "path": "qmoe.moe_prefill per layer (public API, eager) with pinned host inputs and outputs"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "pf_gemm<gate/up> + pf_gemm<down> (+ routing, gather, h packing) per layer"},
+        "gpu_launches": args.steps * L * 6,
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline and world == 1:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import numpy as np
+        import oracle
+        cores = oracle.threads(os.cpu_count())
+        n = min(8, B)
+        t_l = ti[0, 0, :n].cpu().numpy()
+        used = np.unique(t_l)
+        remap = {int(e): i for i, e in enumerate(used)}
+        ti_local = np.vectorize(lambda e: remap[int(e)])(t_l).astype(np.int32)
+        blocks = table.slots[torch.from_numpy(used).to(dev)].cpu().numpy()
+        s2_local = table.s2[0][torch.from_numpy(used).to(dev)].cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.moe_prefill(xs[0, 0, :n].float().cpu().numpy(), ti_local, tv[0, 0, :n].float().cpu().numpy(),
+                           blocks, 0, s2_local)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": n / (dt * L), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} tokens of layer 0 ({len(used)} experts: block dequant + fp32 GEMMs "
+                                          f"+ index_add) in {dt:.1f} s, extrapolated x{L} layers"}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -378,6 +723,10 @@ def main():
         return run_reference(args, rank)
     if args.workload == "prefill":
         return run_prefill(args, rank, world)
+    if args.workload == "gemv":
+        return run_gemv(args, rank, world)
+    if args.workload == "batch-decode":
+        return run_batch_decode(args, rank, world)
 
     import torch
     import qmoe

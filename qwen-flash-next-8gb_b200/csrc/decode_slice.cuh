@@ -293,6 +293,9 @@ __global__ void __launch_bounds__(kLThreads, 1)
       }
     }
   }
+  // re-read the zeroing counter now (the read at entry may precede the last
+  // CTA's count); the value is back by the time phase 2 checks it
+  if (warp == 1 && lane == 0) seen = ld_relaxed_u64(&g_slice_ctr[slot]);
   __syncthreads();  // every warp is done with the gate/up rows: that region now takes the partials
   float* part = reinterpret_cast<float*>(smem + kLSmGu);  // [warp][feature][gate, up]
   if (t == 0) {
@@ -320,12 +323,13 @@ __global__ void __launch_bounds__(kLThreads, 1)
   // hi/lo after a power-of-two prescale for phase 2.
   float hv = 0.f;
   if (threadIdx.x < nf) {
-    float gs = 0.f, us = 0.f;
+    float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
     for (int w = 0; w < kLWarps; ++w) {
-      gs += part[(w * 48 + threadIdx.x) * 2];
-      us += part[(w * 48 + threadIdx.x) * 2 + 1];
+      gs[w & 3] += part[(w * 48 + threadIdx.x) * 2];
+      us[w & 3] += part[(w * 48 + threadIdx.x) * 2 + 1];
     }
-    const float gg = gs * ws_g, uu = us * ws_u;
+    const float gg = ((gs[0] + gs[1]) + (gs[2] + gs[3])) * ws_g, uu = ((us[0] + us[1]) + (us[2] + us[3])) * ws_u;
     hv = gg / (1.0f + expf(-gg)) * uu;
     h[j * kInter + 16 * b0 + threadIdx.x] = hv;
   }
