@@ -36,6 +36,10 @@ TOPK, N_EXPERTS = 10, 512
 # algorithmic bytes of one decode layer: 10 expert blocks + s2 + coef + x (bf16) + out (fp32)
 LAYER_BYTES = TOPK * BLOCK + TOPK * 12 + TOPK * 4 + HID * 2 + HID * 4
 METRIC = "bs1 decode MoE-layer HBM GB/s (48-layer stack, experts resident in HBM)"
+# DRAM bytes (read + written) per launch measured with ncu (profiles/*.md)
+TRAFFIC_DECODE_SLICE = 27.74e6          # moe_decode_slice, one layer (K = 10)
+TRAFFIC_PREFILL_GEMMS = 1.767e9         # pf_gemm<0> + pf_gemm<1>, one config-3 layer
+TRAFFIC_GEMV_RATIO = 10.55e6 / 10.509312e6   # gemv_stream_kernel DRAM bytes / algorithmic bytes
 UNIT = "GB/s"
 
 
@@ -345,7 +349,9 @@ def run_prefill(args, rank, world):
                 "path": "qmoe.moe_prefill (public API) with pinned host inputs and output"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": tflops / tc_peak, "peak_kind": tc_kind,
-                     "hbm_frac": gbs / peaks()[0], "traffic": None,
+                     "hbm_frac": gbs / peaks()[0],
+                     # the two GEMMs' DRAM bytes per layer, profiles/pf_gemm_prefill-layer.md
+                     "traffic": TRAFFIC_PREFILL_GEMMS if world == 1 and args.tokens == 2048 else None,
                      "kernel": "pf_gemm<gate/up> + pf_gemm<down> (+ routing, gather, h packing)"},
         "gpu_launches": args.steps * 6,
         "clocks": clk.summary(),
@@ -522,7 +528,10 @@ def run_gemv(args, rank, world):
                 "steps": E, "us_per_call": ms_e2e * 1e3 / E,
                 "path": "fp8gemv.gemv (public API, eager) with x from pinned host memory and y copied back"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "kernel": "gemv_stream_kernel", "traffic": None,
+                     "peak_kind": peak_kind, "kernel": "gemv_stream_kernel",
+                     # profiles/gemv_stream_fp8-gemv.md captured the 2560x4096 shape (10.55 MB per
+                     # launch for 10.51 MB algorithmic); scaled to this shape by its bytes
+                     "traffic": TRAFFIC_GEMV_RATIO * b0,
                      "per_launch_bytes": b0},
         "gpu_launches": args.steps * GEMV_CALLS,
         "clocks": clk_summary,
@@ -843,7 +852,10 @@ def main():
                      "kernel": {0: "moe_decode_slice", 4: "moe_decode_slice", 3: "moe_decode_stream",
                                 2: "moe_gate_up_generic + moe_down_generic", 1: "moe_decode_persistent"}
                      .get(args.variant, "?") + " (one launch per decode layer)",
-                     "traffic": None, "per_launch_bytes": LAYER_BYTES},
+                     # DRAM bytes read + written per launch in the ncu capture of
+                     # profiles/moe_decode_slice_decode-layer.md (same layer shape)
+                     "traffic": TRAFFIC_DECODE_SLICE if args.variant in (0, 4) else None,
+                     "per_launch_bytes": LAYER_BYTES},
         "gpu_launches": args.steps * L,
         "clocks": clk.summary(),
     }
