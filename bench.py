@@ -59,6 +59,12 @@ def parse():
                    help="decode: config 2 (default, the headline line); prefill: config 3; gemv: config 1; "
                         "batch-decode: config 4")
     p.add_argument("--batch", type=int, default=64, help="batch-decode: tokens per GPU per step (config 4: 64)")
+    p.add_argument("--ep-mode", default="auto", choices=["auto", "a2a", "ag"],
+                   help="expert-parallel exchange under torchrun: a2a = all-to-all of routed rows (host sync "
+                        "for split sizes), ag = all-gather + reduce-scatter (graph-capturable); auto = ag for "
+                        "batch-decode, a2a for prefill")
+    p.add_argument("--ep-graph", action="store_true",
+                   help="batch-decode with --ep-mode ag: capture each step (NCCL collectives included) in a CUDA graph")
     p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
     p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
     p.add_argument("--variant", type=int, default=0,
@@ -263,10 +269,14 @@ def run_prefill(args, rank, world):
     distinct = [int(torch.unique(t).numel()) for t in tis]
     layer_bytes = [d * BLOCK + T * HID * 2 + T * HID * 4 for d in distinct]
 
+    ep_fn = None
+    if shard is not None:
+        ep_fn = ep.moe_prefill_ep_ag if args.ep_mode == "ag" else ep.moe_prefill_ep
+
     def step(i):
         if shard is None:
             return qmoe.moe_prefill(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0)
-        return ep.moe_prefill_ep(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0, shard)
+        return ep_fn(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0, shard)
 
     def barrier():
         if dist is not None:
@@ -312,7 +322,7 @@ def run_prefill(args, rank, world):
         if shard is None:
             y = qmoe.moe_prefill(d_x, d_ti, d_tv, table.slots, s2, 0)
         else:
-            y = ep.moe_prefill_ep(d_x, d_ti, d_tv, table.slots, s2, 0, shard)
+            y = ep_fn(d_x, d_ti, d_tv, table.slots, s2, 0, shard)
         h_out.copy_(y, non_blocking=True)
 
     E = min(args.e2e_steps, args.steps)
@@ -597,9 +607,13 @@ def run_batch_decode(args, rank, world):
     ti, tv = ti.view(R, L, B, TOPK).contiguous(), tv.view(R, L, B, TOPK).contiguous()
     distinct = [[int(torch.unique(ti[r, l]).numel()) for l in range(L)] for r in range(R)]
 
+    mode = "ag" if args.ep_mode == "auto" else args.ep_mode
+
     def layer(x, t, v, l):
         if shard is None:
             return qmoe.moe_prefill(x, t, v, table.slots, table.s2[l], l)
+        if mode == "ag":
+            return ep.moe_prefill_ep_ag(x, t, v, table.slots, table.s2[l], l, shard)
         return ep.moe_prefill_ep(x, t, v, table.slots, table.s2[l], l, shard)
 
     def step(r):
@@ -607,7 +621,7 @@ def run_batch_decode(args, rank, world):
             layer(xs[r, l], ti[r, l], tv[r, l], l)
 
     graphs = None
-    if shard is None:  # the exchange syncs on the host for its split sizes: EP runs eagerly
+    if shard is None or (mode == "ag" and args.ep_graph):  # the all-to-all exchange syncs on the host
         step(0)
         torch.cuda.synchronize()
         graphs = []
@@ -687,7 +701,9 @@ def run_batch_decode(args, rank, world):
                                f"layer per rank's tokens",
                    "hbm_gbs": gbs, "bytes_per_step": step_bytes,
                    "l2": "no flush: each step reads ~48 GB of distinct expert blocks (>> 126 MB L2)",
-                   "parallelism": f"expert-parallel x{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                   "parallelism": (f"expert-parallel x{world} (NCCL " +
+                                   ("all-gather + reduce-scatter" + (", graph-captured" if graphs else "")
+                                    if mode == "ag" else "all-to-all dispatch/combine") + ")") if world > 1
                    else "single GPU"},
         "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
@@ -718,6 +734,7 @@ def run_batch_decode(args, rank, world):
                                 "sample": f"{n} tokens of layer 0 ({len(used)} experts: block dequant + fp32 GEMMs "
                                           f"+ index_add) in {dt:.1f} s, extrapolated x{L} layers"}
     if dist is not None:
+        del graphs  # graphs holding NCCL calls go before the process group
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

@@ -178,8 +178,10 @@ int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
  *   e = ti[t][k], expert e's block at table[(base + e) * QFN_BLOCK_BYTES].
  *   x:     bf16[T][2560] device, 16-byte aligned.
  *   ti:    [T][topk] device expert ids in [0, n_experts), int64 (torch.topk's
- *          output; ti_is_int64 = 1) or int32.  Pairs with an id outside the
- *          range are skipped and flagged in qfn_prefill_status (bit 2).
+ *          output; ti_is_int64 = 1) or int32.  Pairs with id -1 are skipped
+ *          (expert-parallel callers mark the pairs of other ranks' experts so);
+ *          pairs with any other id outside the range are skipped and flagged
+ *          in qfn_prefill_status (bit 2).
  *   tv:    [T][topk] device routing weights, tv_dtype BF16 or F32.
  *   s2l:   f32[n_experts][3] device (ws2 gate/up/down of the layer's experts).
  *   out:   f32[T][2560] device, 16-byte aligned; written (not accumulated).

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
   for (int64_t p = tid; p < P; p += blockDim.x) {
     const int64_t e = static_cast<int64_t>(ti[p]);
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-    else pf_flag(kPfStatusBadExpert);
+    else if (e != -1) pf_flag(kPfStatusBadExpert);  // -1 marks a pair to skip (expert-parallel padding)
   }
   __syncthreads();
   const int c = tid < E ? cnt[tid] : 0;

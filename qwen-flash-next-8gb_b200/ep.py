@@ -19,6 +19,14 @@ The result on each rank equals the single-GPU qmoe.moe_prefill of its tokens
 (the reference's expert loop, qwen_engine.py:835-852) to fp32 accumulation
 order.  Collectives run on the given process group (NCCL between GPUs; gloo
 works for CPU tensors).  Batched decode uses the same exchange.
+
+moe_prefill_ep_ag is the second exchange: every rank all-gathers all ranks'
+tokens (x, expert ids, weights: fixed sizes), runs the grouped GEMM over all
+of them with the pairs of other ranks' experts marked -1 (skipped), and a
+reduce-scatter returns each rank the fp32 sums of its own tokens.  No split
+sizes and no host synchronisation: a layer of it can be captured in a CUDA
+graph.  It moves every token to every rank, so it suits small batches
+(batched decode); the all-to-all exchange moves only routed rows.
 """
 import torch
 import torch.distributed as dist
@@ -90,4 +98,33 @@ def moe_prefill_ep(x, ti, tv, table, s2, L, shard, group=None, compute=None):
     _a2a(y_back, y.contiguous(), send_splits, recv_splits, group)
     out = torch.zeros(T, x.shape[1], dtype=torch.float32, device=dev)
     out.index_add_(0, tok, y_back)
+    return out
+
+
+def moe_prefill_ep_ag(x, ti, tv, table, s2, L, shard, group=None, compute=None):
+    """Expert-parallel MoE layer through all-gather + reduce-scatter (no host sync).
+
+    Arguments as moe_prefill_ep; every rank passes the same number of tokens T.
+    `compute(x_all, ti_local [N*T, topk] (-1 = another rank's expert), tv_all,
+    table, s2, L)` defaults to qmoe.moe_prefill.
+    """
+    compute = compute or qmoe.moe_prefill
+    N = shard.world
+    T, K = ti.shape
+    dev = x.device
+    x_all = torch.empty(N * T, x.shape[1], dtype=x.dtype, device=dev)
+    dist.all_gather_into_tensor(x_all, x.contiguous(), group=group)
+    meta = torch.cat([ti.to(torch.int32), tv.float().contiguous().view(torch.int32)], 1).contiguous()
+    meta_all = torch.empty(N * T, 2 * K, dtype=torch.int32, device=dev)
+    dist.all_gather_into_tensor(meta_all, meta, group=group)
+    local = meta_all[:, :K] - shard.first
+    ti_loc = torch.where((local >= 0) & (local < shard.per_rank), local, torch.full_like(local, -1)).contiguous()
+    tv_all = meta_all[:, K:].contiguous().view(torch.float32)
+    y_all = compute(x_all, ti_loc, tv_all, table, s2, L)
+    out = torch.empty(T, x.shape[1], dtype=torch.float32, device=dev)
+    if dist.get_backend(group) == "gloo":          # gloo has no reduce_scatter_tensor
+        dist.all_reduce(y_all, group=group)
+        out.copy_(y_all[shard.rank * T:(shard.rank + 1) * T])
+    else:
+        dist.reduce_scatter_tensor(out, y_all, group=group)
     return out

@@ -42,7 +42,15 @@ def _cpu_compute(x_pairs, e_local, w, table, s2, L):
     return torch.from_numpy(out)
 
 
-def _worker(rank, port, results):
+def _cpu_compute_ag(x_all, ti_loc, tv_all, table, s2, L):
+    # pairs of other ranks' experts are marked -1: give them weight 0 on expert 0
+    ti = ti_loc.numpy().astype(np.int32)
+    w = np.where(ti >= 0, tv_all.numpy(), 0.0).astype(np.float32)
+    out = oracle.moe_prefill(x_all.float().numpy(), np.maximum(ti, 0), w, table.numpy(), L * s2.shape[0], s2.numpy())
+    return torch.from_numpy(out)
+
+
+def _worker(rank, port, results, mode="a2a"):
     import ep
     os.environ["GLOO_SOCKET_IFNAME"] = "lo"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD)
@@ -51,15 +59,17 @@ def _worker(rank, port, results):
         shard = ep.ExpertShard(E, WORLD, rank)
         own = slice(shard.first, shard.first + shard.per_rank)
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
-        out = ep.moe_prefill_ep(torch.from_numpy(x[toks]), torch.from_numpy(ti[toks]).long(),
-                                torch.from_numpy(tv[toks]), torch.from_numpy(blocks[own]),
-                                torch.from_numpy(s2[own]), 0, shard, compute=_cpu_compute)
+        fn, compute = (ep.moe_prefill_ep, _cpu_compute) if mode == "a2a" else (ep.moe_prefill_ep_ag, _cpu_compute_ag)
+        out = fn(torch.from_numpy(x[toks]), torch.from_numpy(ti[toks]).long(), torch.from_numpy(tv[toks]),
+                 torch.from_numpy(blocks[own]), torch.from_numpy(s2[own]), 0, shard, compute=compute)
         results[rank] = out.numpy()
     finally:
         dist.destroy_process_group()
 
 
-def test_expert_parallel_prefill_matches_single_process():
+@pytest.mark.parametrize("mode", ["a2a", "ag"])
+def test_expert_parallel_prefill_matches_single_process(mode):
+    """mode a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter."""
     blocks, s2, x, ti, tv = _inputs()
     # both ranks really exchange: some pairs of each rank's tokens live on the other rank
     owners = ti // (E // WORLD)
@@ -69,7 +79,7 @@ def test_expert_parallel_prefill_matches_single_process():
     with ctx.Manager() as m:
         results = m.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        procs = [ctx.Process(target=_worker, args=(r, port, results, mode)) for r in range(WORLD)]
         for p in procs:
             p.start()
         for p in procs:

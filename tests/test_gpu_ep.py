@@ -32,7 +32,7 @@ def _inputs():
     return blocks, s2, x, ti, tv
 
 
-def _worker(rank, port, results):
+def _worker(rank, port, results, mode="a2a"):
     import datetime
     import torch.distributed as dist
     import ep
@@ -46,9 +46,10 @@ def _worker(rank, port, results):
         shard = ep.ExpertShard(E, WORLD, rank)
         own = slice(shard.first, shard.first + shard.per_rank)
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
-        out = ep.moe_prefill_ep(x[toks].to(dev), torch.from_numpy(ti[toks]).long().to(dev),
-                                torch.from_numpy(tv[toks]).to(dev).to(torch.bfloat16),
-                                torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0, shard)
+        fn = ep.moe_prefill_ep if mode == "a2a" else ep.moe_prefill_ep_ag
+        out = fn(x[toks].to(dev), torch.from_numpy(ti[toks]).long().to(dev),
+                 torch.from_numpy(tv[toks]).to(dev).to(torch.bfloat16),
+                 torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0, shard)
         torch.cuda.synchronize()
         results[rank] = out.cpu().numpy()
         dist.barrier()
@@ -57,7 +58,10 @@ def _worker(rank, port, results):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_expert_parallel_prefill_two_gpus_matches_oracle():
+@pytest.mark.parametrize("mode", ["a2a", "ag"])
+def test_expert_parallel_prefill_two_gpus_matches_oracle(mode):
+    """a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter (pairs of
+    the other rank's experts passed to the grouped GEMM as -1)."""
     import torch.multiprocessing as mp
     blocks, s2, x, ti, tv = _inputs()
     ref = oracle.moe_prefill(x.float().numpy(), ti, tv, blocks, 0, s2)
@@ -65,7 +69,7 @@ def test_expert_parallel_prefill_two_gpus_matches_oracle():
     with ctx.Manager() as m:
         results = m.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        procs = [ctx.Process(target=_worker, args=(r, port, results, mode)) for r in range(WORLD)]
         for p in procs:
             p.start()
         for p in procs:
