@@ -97,21 +97,10 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
   const int64_t P = T * topk;
   for (int i = tid; i < E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
-  // Counting and scattering use warp-aggregated atomics: the lanes of a warp
-  // that hold the same expert (popular experts under skewed routing) make one
-  // shared-memory atomic between them.
-  const int lane = tid & 31;
-  const uint32_t lt = (1u << lane) - 1u;
-  for (int64_t base = 0; base < P; base += blockDim.x) {
-    const int64_t p = base + tid;
-    int e = -2;  // -2: no pair (past the end)
-    if (p < P) {
-      const int64_t v = static_cast<int64_t>(ti[p]);
-      if (v >= 0 && v < E) e = static_cast<int>(v);
-      else if (v != -1) pf_flag(kPfStatusBadExpert);  // -1 marks a pair to skip (expert-parallel padding)
-    }
-    const uint32_t same = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (same & lt) == 0) atomicAdd(&cnt[e], __popc(same));
+  for (int64_t p = tid; p < P; p += blockDim.x) {
+    const int64_t e = static_cast<int64_t>(ti[p]);
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    else if (e != -1) pf_flag(kPfStatusBadExpert);  // -1 marks a pair to skip (expert-parallel padding)
   }
   __syncthreads();
   const int c = tid < E ? cnt[tid] : 0;
@@ -134,20 +123,10 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
     hdr[1] = np;
   }
   __syncthreads();
-  for (int64_t base = 0; base < P; base += blockDim.x) {
-    const int64_t p = base + tid;
-    int e = -2;
-    if (p < P) {
-      const int64_t v = static_cast<int64_t>(ti[p]);
-      if (v >= 0 && v < E) e = static_cast<int>(v);
-    }
-    const uint32_t same = __match_any_sync(0xffffffffu, e);
-    const int leader = __ffs(same) - 1;
-    int pos0 = 0;
-    if (e >= 0 && lane == leader) pos0 = atomicAdd(&cur[e], __popc(same));
-    pos0 = __shfl_sync(0xffffffffu, pos0, leader);
-    if (e < 0) continue;
-    const int pos = pos0 + __popc(same & lt);
+  for (int64_t p = tid; p < P; p += blockDim.x) {
+    const int64_t e = static_cast<int64_t>(ti[p]);
+    if (e < 0 || e >= E) continue;
+    const int pos = atomicAdd(&cur[e], 1);
     pair_tok[pos] = static_cast<int>(p / topk);
     float w;
     if (kTvBf16) w = bf16_bits_to_f32(static_cast<const uint16_t*>(tv)[p]);
