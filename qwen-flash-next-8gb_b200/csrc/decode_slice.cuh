@@ -15,11 +15,12 @@
 // all 2,560 down rows.  Nothing crosses CTAs except the final sum over the
 // CTAs' partial output vectors, done with fp32 vector atomics into `out`.
 //
-// Copies: per block one 4-D TMA box of its 16 gate + 16 up rows (40 KB) and
-// one of their scale rows (5 KB); the down column slice as two 4-D boxes of
-// 1,280 rows x 32 bytes (the 16-byte aligned cover of the 16-24 needed
-// bytes).  The down scales (1-3 bytes of each 40-byte row) are gathered with
-// 32-bit loads.  8 TMA copies per CTA, in two waves: blocks 0 and 1 at entry,
+// Copies: per block four contiguous bulk copies (its 16 gate rows, 16 up
+// rows, 20 KB each, and their two 2.5 KB scale runs; 4-D tensor boxes of the
+// same bytes streamed measurably slower); the down column slice as two 4-D
+// TMA boxes of 1,280 rows x 32 bytes (the 16-byte aligned cover of the 16-24
+// needed bytes).  The down scales (1-3 bytes of each 40-byte row) are
+// gathered with 32-bit loads.  Copies go out in two waves: blocks 0 and 1 at entry,
 // the rest once block 0 has landed.  Issued all at once, every copy would
 // complete near the end of the layer's whole stream (HBM serves the queued
 // requests in no particular order) and the arithmetic could not overlap it.
@@ -93,8 +94,7 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 
 template <bool kXF32>
 __global__ void __launch_bounds__(kLThreads, 1)
-    moe_decode_slice(const __grid_constant__ CUtensorMap gu_map, const __grid_constant__ CUtensorMap gs_map,
-                     const __grid_constant__ CUtensorMap dn_map, const uint8_t* __restrict__ table, int64_t n_blocks,
+    moe_decode_slice(const __grid_constant__ CUtensorMap dn_map, const uint8_t* __restrict__ table, int64_t n_blocks,
                      const int32_t* __restrict__ sidx, const float* __restrict__ s2, const float* __restrict__ coef,
                      const void* __restrict__ x, float* __restrict__ h, float* __restrict__ out, int K, int slot) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -117,8 +117,6 @@ __global__ void __launch_bounds__(kLThreads, 1)
     fence_mbar_init();
   }
   if (threadIdx.x == 32) {
-    prefetch_tensormap(&gu_map);
-    prefetch_tensormap(&gs_map);
     prefetch_tensormap(&dn_map);
   }
   __syncthreads();
@@ -144,8 +142,12 @@ __global__ void __launch_bounds__(kLThreads, 1)
   auto issue_gu = [&](int b) {
     const int f0 = 16 * (b0 + b);
     mbar_arrive_expect_tx(&bar[b], kLGuBytes + kLGsBytes);
-    tma_load_4d(smem + kLSmGu + b * kLGuBytes, &gu_map, 0, f0, 0, static_cast<int>(blk), &bar[b]);
-    tma_load_4d(smem + kLSmGs + b * kLGsBytes, &gs_map, 0, f0, 0, static_cast<int>(blk), &bar[b]);
+    uint8_t* gu = smem + kLSmGu + b * kLGuBytes;
+    uint8_t* gs = smem + kLSmGs + b * kLGsBytes;
+    bulk_g2s(gu, eb + kOGW + f0 * (kHid / 2), kLGuBytes / 2, &bar[b]);
+    bulk_g2s(gu + kLGuBytes / 2, eb + kOUW + f0 * (kHid / 2), kLGuBytes / 2, &bar[b]);
+    bulk_g2s(gs, eb + kOGS + f0 * (kHid / 16), kLGsBytes / 2, &bar[b]);
+    bulk_g2s(gs + kLGsBytes / 2, eb + kOUS + f0 * (kHid / 16), kLGsBytes / 2, &bar[b]);
   };
   auto issue_wave_b = [&]() {
     if (nb > 2) issue_gu(2);
@@ -412,20 +414,8 @@ inline bool slice_fits(int K, const DeviceInfo* dev) {
 inline int launch_moe_decode_slice(const uint8_t* table, int64_t n_blocks, const int32_t* sidx, const float* s2,
                                    const float* coef, const void* x, int x_dtype, float* h_buf, float* out, int K,
                                    cudaStream_t st, const DeviceInfo* dev) {
-  CUtensorMap gu_map, gs_map, dn_map;
+  CUtensorMap dn_map;
   const uint64_t nbk = static_cast<uint64_t>(n_blocks);
-  {  // gate | up rows as u64 words: [block][gate, up][640 rows][160 words]
-    const uint64_t dims[4] = {160, 640, 2, nbk}, strides[3] = {1280, 819200, static_cast<uint64_t>(kBlock)};
-    const uint32_t box[4] = {160, 16, 2, 1};
-    int rc = tensor_map_nd(table + kOGW, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, dims, strides, box, dev->device, &gu_map);
-    if (rc) return rc;
-  }
-  {  // gate | up scale rows: [block][gate_s, up_s][640 rows][20 words]
-    const uint64_t dims[4] = {20, 640, 2, nbk}, strides[3] = {160, 102400, static_cast<uint64_t>(kBlock)};
-    const uint32_t box[4] = {20, 16, 2, 1};
-    int rc = tensor_map_nd(table + kOGS, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, dims, strides, box, dev->device, &gs_map);
-    if (rc) return rc;
-  }
   {  // down rows as bytes: [block][10 row groups][256 rows][320 B]
     const uint64_t dims[4] = {320, 256, 10, nbk}, strides[3] = {320, 81920, static_cast<uint64_t>(kBlock)};
     const uint32_t box[4] = {32, 256, 5, 1};
@@ -457,7 +447,7 @@ inline int launch_moe_decode_slice(const uint8_t* table, int64_t n_blocks, const
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, gu_map, gs_map, dn_map, table, n_blocks, sidx, s2, coef, x, h_buf,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, dn_map, table, n_blocks, sidx, s2, coef, x, h_buf,
                                      out, K, slot);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_decode_slice launch: %s", cudaGetErrorString(e));
   return check_launch("moe_decode_slice");
