@@ -20,7 +20,7 @@
 // same bytes streamed measurably slower); the down column slice as two 4-D
 // TMA boxes of 1,280 rows x 32 bytes (the 16-byte aligned cover of the 16-24
 // needed bytes).  The down scales (1-3 bytes of each 40-byte row) are
-// gathered with 32-bit loads.  Copies go out in two waves: blocks 0 and 1 at entry,
+// gathered with 32-bit loads once block 0 has landed.  Copies go out in two waves: blocks 0 and 1 at entry,
 // the rest once block 0 has landed.  Issued all at once, every copy would
 // complete near the end of the layer's whole stream (HBM serves the queued
 // requests in no particular order) and the arithmetic could not overlap it.
@@ -234,11 +234,13 @@ __global__ void __launch_bounds__(kLThreads, 1)
   if (warp == 1 && lane == 0) seen = ld_relaxed_u64(&g_slice_ctr[slot]);  // usually final by the time it is checked
 
   // The down scales of this CTA's blocks: bytes [b0, b1) of every 40-byte row,
-  // gathered by warps 2-19 as one or two aligned words per row; the values
-  // are stored after block 0's phase 1, so no warp waits for the loads.
+  // gathered by warps 2-19 as one or two aligned words per row.  The loads go
+  // out once block 0 has landed (by then the L2 prefetch of the expert's
+  // down scales issued at entry has brought them in; issued at entry they
+  // queue behind the layer's stream) and are stored after phase 1.
   constexpr int kGN = kLThreads - 64, kGIt = (kHid + kGN - 1) / kGN;
   uint32_t wa[kGIt], wb[kGIt];
-  if (ok && warp >= 2) {
+  auto gather_scales = [&]() {
     const uint8_t* ds = eb + kODS + (b0 & ~3);
     const bool two = (b0 & 3) + nb > 4;
 #pragma unroll
@@ -248,7 +250,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
       wa[i] = __ldg(q);
       wb[i] = two ? __ldg(q + 1) : 0u;
     }
-  }
+  };
 
   // Wait (bounded, warp 1 lane 0) until every CTA of this call has zeroed its
   // share of out; the caller follows with a block barrier.
@@ -278,6 +280,11 @@ __global__ void __launch_bounds__(kLThreads, 1)
     if (b < nbl) {
       if (!mbar_wait(&bar[b], 0)) note_timeout();
       if (warp == 0 && b == 0 && nb > 1 && lane == 0) issue_wave_b();
+      // re-read the zeroing counter once block 0 is in (the read at entry may
+      // precede the last CTA's count; under the layer's stream a load takes
+      // microseconds, so it is issued long before its use)
+      if (warp == 1 && b == 0 && lane == 0) seen = ld_relaxed_u64(&g_slice_ctr[slot]);
+      if (warp >= 2 && b == 0) gather_scales();
       const uint8_t* gu = smem + kLSmGu + b * kLGuBytes;
       const uint8_t* gs = smem + kLSmGs + b * kLGsBytes;
 #pragma unroll
@@ -295,9 +302,9 @@ __global__ void __launch_bounds__(kLThreads, 1)
       }
     }
   }
-  // re-read the zeroing counter now (the read at entry may precede the last
-  // CTA's count); the value is back by the time phase 2 checks it
-  if (warp == 1 && lane == 0) seen = ld_relaxed_u64(&g_slice_ctr[slot]);
+  // one more read if that one was early too
+  if (warp == 1 && lane == 0 && seen < (ticket / static_cast<unsigned long long>(G) + 1ull) * G)
+    seen = ld_relaxed_u64(&g_slice_ctr[slot]);
   __syncthreads();  // every warp is done with the gate/up rows: that region now takes the partials
   float* part = reinterpret_cast<float*>(smem + kLSmGu);  // [warp][feature][gate, up]
   if (t == 0) {

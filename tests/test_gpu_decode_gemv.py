@@ -214,7 +214,8 @@ def test_gemv_matches_reference_golden(golden, N, K):
     check_bf16(fp8gemv.gemv(qd, cuda(s), x.to(DEV)), y32, oracle.gemv(q, s, x.float().numpy()))
 
 
-@pytest.mark.parametrize("N,K", [(13, 48), (1, 16), (10240, 2560), (6144, 2560), (2560, 6144), (33, 32768)])
+@pytest.mark.parametrize("N,K", [(13, 48), (1, 16), (10240, 2560), (6144, 2560), (2560, 6144), (33, 32768),
+                                 (3, 64), (100, 1024), (150, 2560), (20480, 4096)])
 def test_gemv_matches_oracle_odd_shapes(N, K):
     q, s, x = gemv_inputs(N, K, N + K, K)
     qd = cuda(q).view(torch.float8_e4m3fn)
