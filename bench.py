@@ -779,7 +779,7 @@ def main():
             if outs is not None:
                 outs.append(y)
 
-    # one CUDA graph per routed step (48 layers x 2 kernels each)
+    # one CUDA graph per routed step (one kernel per layer)
     step_eager(0)
     torch.cuda.synchronize()
     pool = torch.cuda.graph_pool_handle()

@@ -318,13 +318,6 @@ __global__ void __launch_bounds__(kLThreads, 1)
           part[(warp * 48 + f) * 2 + 1] = pu[2 * b + o];
         }
   }
-  if (warp >= 2) {
-#pragma unroll
-    for (int i = 0; i < kGIt; ++i) {
-      const int r = threadIdx.x - 64 + i * kGN;
-      if (r < kHid) dsc[r] = __funnelshift_r(wa[i], wb[i], 8 * (b0 & 3));
-    }
-  }
   __syncthreads();
 
   // h of this CTA's features (the reference's formula; the warps' partials
@@ -340,7 +333,6 @@ __global__ void __launch_bounds__(kLThreads, 1)
     }
     const float gg = ((gs[0] + gs[1]) + (gs[2] + gs[3])) * ws_g, uu = ((us[0] + us[1]) + (us[2] + us[3])) * ws_u;
     hv = gg / (1.0f + expf(-gg)) * uu;
-    h[j * kInter + 16 * b0 + threadIdx.x] = hv;
   }
   float* wred = reinterpret_cast<float*>(misc + 640);  // [2] warp maxima of |h|
   if (warp < 2) {
@@ -351,6 +343,16 @@ __global__ void __launch_bounds__(kLThreads, 1)
   }
   wait_zeroed();  // phase 2 adds into out tile by tile
   __syncthreads();
+  // After the wait: its fence would otherwise wait for this store (warp 1
+  // holds features 32-47), and the scale stores wait for their gathers.
+  if (threadIdx.x < nf) h[j * kInter + 16 * b0 + threadIdx.x] = hv;
+  if (warp >= 2) {
+#pragma unroll
+    for (int i = 0; i < kGIt; ++i) {
+      const int r = threadIdx.x - 64 + i * kGN;
+      if (r < kHid) dsc[r] = __funnelshift_r(wa[i], wb[i], 8 * (b0 & 3));
+    }
+  }
   const int eh = f16_prescale_exp(nanmax(wred[0], wred[1]));
   if (threadIdx.x < nf) split_f16(scale_pow2(hv, eh), hhi[threadIdx.x], hlo[threadIdx.x]);
   __syncthreads();
