@@ -61,10 +61,7 @@ def parse():
     p.add_argument("--batch", type=int, default=64, help="batch-decode: tokens per GPU per step (config 4: 64)")
     p.add_argument("--ep-mode", default="auto", choices=["auto", "a2a", "ag"],
                    help="expert-parallel exchange under torchrun: a2a = all-to-all of routed rows (host sync "
-                        "for split sizes), ag = all-gather + reduce-scatter (graph-capturable); auto = ag for "
-                        "batch-decode, a2a for prefill")
-    p.add_argument("--ep-graph", action="store_true",
-                   help="batch-decode with --ep-mode ag: capture each step (NCCL collectives included) in a CUDA graph")
+                        "for split sizes), ag = all-gather + reduce-scatter (no host sync); auto = ag")
     p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
     p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
     p.add_argument("--variant", type=int, default=0,
@@ -271,7 +268,7 @@ def run_prefill(args, rank, world):
 
     ep_fn = None
     if shard is not None:
-        ep_fn = ep.moe_prefill_ep_ag if args.ep_mode == "ag" else ep.moe_prefill_ep
+        ep_fn = ep.moe_prefill_ep if args.ep_mode == "a2a" else ep.moe_prefill_ep_ag
 
     def step(i):
         if shard is None:
@@ -352,7 +349,9 @@ def run_prefill(args, rank, world):
                    "tflops": tflops, "hbm_gbs": gbs, "bytes_per_step": avg_bytes,
                    "flop_per_step": pairs * PF_FLOP_PER_PAIR,
                    "l2": "no flush: each step reads >= 1.4 GB of distinct expert blocks (> 126 MB L2)",
-                   "parallelism": f"expert-parallel x{world} (NCCL all-to-all dispatch/combine)" if world > 1
+                   "parallelism": (f"expert-parallel x{world} (NCCL "
+                                   + ("all-to-all dispatch/combine" if args.ep_mode == "a2a"
+                                      else "all-gather + reduce-scatter") + ")") if world > 1
                    else "single GPU"},
         "e2e": {"value": world * T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
@@ -621,7 +620,7 @@ def run_batch_decode(args, rank, world):
             layer(xs[r, l], ti[r, l], tv[r, l], l)
 
     graphs = None
-    if shard is None or (mode == "ag" and args.ep_graph):  # the all-to-all exchange syncs on the host
+    if shard is None:  # expert-parallel steps run eagerly (NCCL collectives are not captured)
         step(0)
         torch.cuda.synchronize()
         graphs = []
@@ -702,8 +701,8 @@ def run_batch_decode(args, rank, world):
                    "hbm_gbs": gbs, "bytes_per_step": step_bytes,
                    "l2": "no flush: each step reads ~48 GB of distinct expert blocks (>> 126 MB L2)",
                    "parallelism": (f"expert-parallel x{world} (NCCL " +
-                                   ("all-gather + reduce-scatter" + (", graph-captured" if graphs else "")
-                                    if mode == "ag" else "all-to-all dispatch/combine") + ")") if world > 1
+                                   ("all-gather + reduce-scatter" if mode == "ag" else "all-to-all dispatch/combine")
+                                   + ")") if world > 1
                    else "single GPU"},
         "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
