@@ -55,9 +55,9 @@ def parse():
     p.add_argument("--cpu-layers", type=int, default=4, help="layers timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "gemv", "batch-decode"],
+    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "gemv", "batch-decode", "fp8-linear"],
                    help="decode: config 2 (default, the headline line); prefill: config 3; gemv: config 1; "
-                        "batch-decode: config 4")
+                        "batch-decode: config 4; fp8-linear: the FP8 linear layer for T > 1 tokens")
     p.add_argument("--batch", type=int, default=64, help="batch-decode: tokens per GPU per step (config 4: 64)")
     p.add_argument("--ep-mode", default="auto", choices=["auto", "a2a", "ag"],
                    help="expert-parallel exchange under torchrun: a2a = all-to-all of routed rows (host sync "
@@ -740,6 +740,124 @@ def run_batch_decode(args, rank, world):
         print(json.dumps(line))
 
 
+LIN_COPIES = 4                                 # weight copies per shape, rotated (4 x 42 MB > 126 MB L2)
+
+
+def run_fp8_linear(args, rank, world):
+    """The engine's FP8 linear layer for T > 1 tokens (Lin.__call__,
+    qwen_engine.py:79-83): --tokens (2048) tokens through the config-1 shapes
+    (12288x2560 and 2560x4096); a step = one call per shape through
+    fp8gemv.linear (this library's e4m3 -> bf16 kernel + the bf16 GEMM).  Also
+    timed on the same stream: the e4m3 -> bf16 kernel alone (its HBM roofline)
+    and the reference's own torch expression F.linear(x, (q.to(bf16) * s).to(bf16)).
+    N GPUs: replicas."""
+    import torch
+    import torch.nn.functional as F
+    import fp8gemv
+    import synthetic
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    T = args.tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 31)
+    data = {}
+    for (N, K) in GEMV_SHAPES:
+        qs, ss = [], []
+        for _ in range(LIN_COPIES):
+            w = torch.randn(N, K, device=dev, generator=g) * 0.02
+            q, sc = synthetic.to_fp8_rows(w)
+            qs.append(q.contiguous())
+            ss.append(sc.view(-1, 1).contiguous())
+            del w
+        data[(N, K)] = (qs, ss, torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16))
+
+    def ours(i):
+        return [fp8gemv.linear(x, qs[i % LIN_COPIES], ss[i % LIN_COPIES]) for qs, ss, x in data.values()]
+
+    def deq_only(i):
+        for qs, ss, _ in data.values():
+            fp8gemv.dequant_bf16(qs[i % LIN_COPIES], ss[i % LIN_COPIES])
+
+    def reference(i):
+        for qs, ss, x in data.values():
+            q, sc = qs[i % LIN_COPIES], ss[i % LIN_COPIES]
+            F.linear(x, (q.to(torch.bfloat16) * sc).to(torch.bfloat16))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    st = torch.cuda.current_stream()
+
+    def timed(fn, clk=None):
+        for i in range(max(args.warmup, 3)):
+            fn(i)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(args.steps):
+            fn(i)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if dist is not None:
+            t_ = torch.tensor([ms], device=dev)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            ms = float(t_.item())
+        return ms
+
+    with ClockSampler(local) as clk:
+        ms = timed(ours)
+    ms_deq = timed(deq_only)
+    ms_ref = timed(reference)
+
+    # e2e: the public call with x copied in from pinned host memory and y read back, every step
+    hx = {k: v[2].cpu().pin_memory() for k, v in data.items()}
+    hy = {(N, K): torch.empty(T, N, dtype=torch.bfloat16).pin_memory() for (N, K) in GEMV_SHAPES}
+    dx = {k: torch.empty_like(v[2]) for k, v in data.items()}
+
+    def e2e(i):
+        for k, (qs, ss, _) in data.items():
+            dx[k].copy_(hx[k], non_blocking=True)
+            hy[k].copy_(fp8gemv.linear(dx[k], qs[i % LIN_COPIES], ss[i % LIN_COPIES]), non_blocking=True)
+
+    ms_e2e = timed(e2e)
+    flop = sum(2 * T * N * K for (N, K) in GEMV_SHAPES)
+    deq_bytes = sum(3 * N * K + 4 * N for (N, K) in GEMV_SHAPES)
+    value = world * flop / (ms * 1e-3) / 1e12
+    hbm, hbm_kind = peaks()
+    deq_gbs = deq_bytes / (ms_deq * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"fp8 linear layer, T={T} tokens, TFLOP/s (config-1 weight shapes)", "value": value,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 weights -> bf16, bf16 GEMM, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"fp8-linear: {T} tokens x (12288x2560 + 2560x4096), bf16 out",
+                       "us_reference_expression_same_gpu": ms_ref * 1e3, "us_dequant_kernel": ms_deq * 1e3,
+                       "l2": f"no flush: {LIN_COPIES} rotated weight copies per shape (> 126 MB L2)",
+                       "parallelism": "single GPU" if world == 1 else f"{world} replicas"},
+            "e2e": {"value": world * flop / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(T * K * 2 for (N, K) in GEMV_SHAPES),
+                    "d2h_bytes_per_step": sum(T * N * 2 for (N, K) in GEMV_SHAPES), "ms_per_step": ms_e2e,
+                    "path": "fp8gemv.linear (public API) with pinned host x in and y out"},
+            "roofline": {"bound": "hbm", "achieved": deq_gbs, "peak": hbm, "unit": "GB/s", "frac": deq_gbs / hbm,
+                         "peak_kind": hbm_kind, "traffic": None,
+                         "kernel": "e4m3_rows_to_bf16_kernel (3 B per weight); the GEMM is cuBLAS"},
+            "gpu_launches": args.steps * len(GEMV_SHAPES),
+            "clocks": clk.summary(),
+        }))
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -752,6 +870,8 @@ def main():
         return run_gemv(args, rank, world)
     if args.workload == "batch-decode":
         return run_batch_decode(args, rank, world)
+    if args.workload == "fp8-linear":
+        return run_fp8_linear(args, rank, world)
 
     import torch
     import qmoe

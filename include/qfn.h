@@ -171,6 +171,19 @@ int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
                   int y_dtype, int64_t N, int64_t K, qfn_stream_t stream);
 
 /*
+ * qfn_e4m3_rows_to_bf16 -- replaces the weight expression of the engine's FP8
+ * linear layer for T > 1 tokens (qwen_engine.py:83):
+ *   (q.to(torch.bfloat16) * s).to(torch.bfloat16)
+ *   w[n][k] = bf16_rn(fp32(e4m3(q[n][k])) * s[n])   (bit-identical)
+ *   q: u8[N][K] (float8_e4m3fn bytes) device, 16-byte aligned, K % 16 == 0.
+ *   s: f32[N] device (the [N, 1] row scales).
+ *   w: bf16[N][K] device (raw 16-bit words), 16-byte aligned.
+ * The caller then runs the bf16 GEMM (F.linear(x, w)) as the reference does.
+ */
+int qfn_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* w, int64_t N, int64_t K,
+                          qfn_stream_t stream);
+
+/*
  * qfn_moe_prefill -- the batched-prefill expert loop of QwenEngine.moe
  * (qwen_engine.py:835-852), which the reference runs as a Python loop over
  * experts (block_deq + three fp32 torch GEMMs + index_add_ per expert):

@@ -163,3 +163,19 @@ def bf16_round(a):
     out = r.view(np.float32).copy()
     out[nan] = np.nan
     return out
+
+
+def e4m3_rows_to_bf16(q, s):
+    """qwen_engine.py:83 weight expression, (q.to(bf16) * s).to(bf16), as bf16
+    bit patterns u16[N,K]: e4m3 -> fp32 (exact), one fp32 multiply by the row
+    scale (round to nearest even), fp32 -> bf16 (round to nearest even)."""
+    q, s = _c(q, np.uint8), _c(s, np.float32).reshape(-1)
+    w = e4m3_decode_table()[q] * s[:, None]          # numpy float32 multiply: IEEE, nearest even
+    return (bf16_round(w).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def fp8_linear(x, q, s):
+    """Lin.__call__ for T > 1 (qwen_engine.py:83) in fp32: x [T,K] @ w_bf16.T -> f32[T,N]
+    (the caller rounds to bf16; the GPU GEMM's accumulation order differs)."""
+    w = (e4m3_rows_to_bf16(q, s).astype(np.uint32) << 16).view(np.float32)
+    return _c(x, np.float32) @ w.T

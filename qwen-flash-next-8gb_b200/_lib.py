@@ -28,6 +28,7 @@ SIGNATURES = {
     "qfn_moe_decode_noalloc": [_P, _I64, _P, _P, _P, _P, _I, _P, _I, _P],
     "qfn_device_status": [_P, _I],
     "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
+    "qfn_e4m3_rows_to_bf16": [_P, _P, _P, _I64, _I64, _P],
     "qfn_moe_prefill_workspace": [_I64, _I, _I],
     "qfn_moe_prefill": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P],
     "qfn_prefill_status": [_P, _I],

@@ -341,9 +341,89 @@ static int launch_gemv(const uint8_t* q, const float* s, const uint16_t* x, void
   return check_launch("gemv_e4m3_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// E4M3 rows -> bf16 weights for the T > 1 path of the engine's FP8 linear
+// layer (qwen_engine.py:79-83): F.linear(x, (q.to(bf16) * s).to(bf16)).
+// w[n][k] = bf16_rn(f32(q[n][k]) * s[n]): e4m3 -> bf16 is exact, the product
+// is one fp32 multiply rounded to nearest even, then rounded to bf16 -- the
+// same two roundings as the reference's torch expression, in one pass that
+// reads 1 byte and writes 2 per weight (the torch chain writes a bf16 and an
+// fp32 temporary and reads both back).  A thread takes up to four 16-weight
+// chunks a grid stride apart and issues their loads before any store, so
+// each SM keeps ~128 KB of reads in flight.
+__device__ __forceinline__ void e4m3x16_rows_to_bf16(uint4 v, float sc, uint16_t* __restrict__ w, int64_t c) {
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t lo, hi;
+    e4m3x4_to_f16x2(in[i], lo, hi);
+    const float2 a = f16x2_to_f32x2(lo), b = f16x2_to_f32x2(hi);
+    const __nv_bfloat162 ra = __floats2bfloat162_rn(__fmul_rn(a.x, sc), __fmul_rn(a.y, sc));
+    const __nv_bfloat162 rb = __floats2bfloat162_rn(__fmul_rn(b.x, sc), __fmul_rn(b.y, sc));
+    o[2 * i] = *reinterpret_cast<const uint32_t*>(&ra);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&rb);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(w) + 2 * c;
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+constexpr int kDqUnroll = 4;
+
+__global__ void __launch_bounds__(256) e4m3_rows_to_bf16_kernel(const uint8_t* __restrict__ q,
+                                                                 const float* __restrict__ s,
+                                                                 uint16_t* __restrict__ w, int64_t n_chunks,
+                                                                 int64_t chunks_per_row) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c0 < n_chunks;
+       c0 += kDqUnroll * stride) {
+    uint4 v[kDqUnroll];
+    float sc[kDqUnroll];
+#pragma unroll
+    for (int u = 0; u < kDqUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      if (c < n_chunks) {
+        v[u] = ldg_stream_v4(reinterpret_cast<const uint4*>(q) + c);
+        sc[u] = s[c / chunks_per_row];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kDqUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      if (c < n_chunks) e4m3x16_rows_to_bf16(v[u], sc[u], w, c);
+    }
+  }
+}
+
+static int launch_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* w, int64_t N, int64_t K,
+                                    cudaStream_t st) {
+  DeviceInfo* dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  const int64_t cpr = K / 16, n_chunks = N * cpr;
+  int64_t blocks = (n_chunks + 256 * kDqUnroll - 1) / (256 * kDqUnroll);
+  const int64_t cap = static_cast<int64_t>(dev->sm_count) * 4;  // one wave (48 registers: <= 5 CTAs per SM)
+  if (blocks > cap) blocks = cap;
+  e4m3_rows_to_bf16_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(q, s, w, n_chunks, cpr);
+  return check_launch("e4m3_rows_to_bf16_kernel");
+}
+
 }  // namespace qfn
 
 using namespace qfn;
+
+extern "C" int qfn_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* w, int64_t N, int64_t K,
+                                     qfn_stream_t stream) {
+  QFN_REQUIRE(q && s && w, QFN_ERR_INVALID_ARG, "qfn_e4m3_rows_to_bf16: null pointer");
+  QFN_REQUIRE(N > 0 && K > 0, QFN_ERR_INVALID_ARG, "qfn_e4m3_rows_to_bf16: N=%lld K=%lld must be positive",
+              (long long)N, (long long)K);
+  QFN_REQUIRE(K % 16 == 0, QFN_ERR_UNSUPPORTED, "qfn_e4m3_rows_to_bf16: K=%lld must be a multiple of 16",
+              (long long)K);
+  QFN_REQUIRE(aligned(q, 16) && aligned(w, 16), QFN_ERR_ALIGNMENT,
+              "qfn_e4m3_rows_to_bf16: q and w must be 16-byte aligned");
+  return launch_e4m3_rows_to_bf16(q, s, w, N, K, as_stream(stream));
+}
 
 extern "C" int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y, int y_dtype,
                              int64_t N, int64_t K, qfn_stream_t stream) {

@@ -24,7 +24,7 @@ def declared():
 
 def test_header_declares_entry_points():
     names = declared()
-    for must in ("qfn_moe_decode", "qfn_gemv_e4m3", "qfn_deq", "qfn_block_deq", "qfn_version",
+    for must in ("qfn_moe_decode", "qfn_gemv_e4m3", "qfn_e4m3_rows_to_bf16", "qfn_deq", "qfn_block_deq", "qfn_version",
                  "qfn_strerror", "qfn_last_error"):
         assert must in names
 
@@ -77,6 +77,11 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert lib.qfn_gemv_e4m3(odd, fake, fake, fake, 1, 16, 32, None) == 2
     # deq: K % 32
     assert lib.qfn_deq(fake, fake, ctypes.c_float(1.0), fake, 4, 48, None) == 4
+    # e4m3 rows -> bf16: nulls, sizes, K % 16, alignment
+    assert lib.qfn_e4m3_rows_to_bf16(None, fake, fake, 4, 32, None) == 1
+    assert lib.qfn_e4m3_rows_to_bf16(fake, fake, fake, 0, 32, None) == 1
+    assert lib.qfn_e4m3_rows_to_bf16(fake, fake, fake, 4, 24, None) == 4
+    assert lib.qfn_e4m3_rows_to_bf16(odd, fake, fake, 4, 32, None) == 2
 
 
 def test_python_wrappers_reject_cpu_tensors():
@@ -86,6 +91,8 @@ def test_python_wrappers_reject_cpu_tensors():
     q = torch.zeros(16, 32, dtype=torch.float8_e4m3fn)
     with pytest.raises(ValueError, match="CUDA"):
         fp8gemv.gemv(q, torch.ones(16), torch.zeros(32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        fp8gemv.linear(torch.zeros(4, 32, dtype=torch.bfloat16), q, torch.ones(16, 1))
     with pytest.raises(ValueError, match="CUDA"):
         qmoe.moe_decode(torch.zeros(1, qmoe.BLOCK, dtype=torch.uint8), torch.zeros(1, dtype=torch.int32),
                         torch.zeros(1, 3), torch.zeros(1), torch.zeros(2560), torch.zeros(1, 640),

@@ -256,3 +256,51 @@ def test_route_on_device_matches_oracle():
     assert np.array_equal(ti.cpu().numpy(), oti)
     got = tv.float().cpu().numpy()
     assert np.all(np.abs(got - ocoef) <= np.abs(ocoef) * 2.0 ** -7)
+
+
+# ---------------------------------------------------------------- FP8 linear, T > 1
+def _bits(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("N,K", [(1, 16), (7, 48), (333, 1040), (2560, 4096), (12288, 2560)])
+def test_e4m3_rows_to_bf16_bit_exact(N, K):
+    """The weight expression of qwen_engine.py:83, bit for bit: against the
+    reference's own torch expression on the GPU and against the oracle; every
+    e4m3 byte value occurs (NaN codes included: NaN stays NaN)."""
+    g = torch.Generator().manual_seed(N + K)
+    qb = torch.randint(0, 256, (N, K), dtype=torch.uint8, generator=g)
+    s = torch.rand(N, generator=g) * 1e-3 + 1e-6
+    qd = qb.to(DEV).view(torch.float8_e4m3fn)
+    got = _bits(fp8gemv.dequant_bf16(qd, s.to(DEV)[:, None]))
+    ref = _bits((qd.to(torch.bfloat16) * s.to(DEV)[:, None]).to(torch.bfloat16))
+    orc = oracle.e4m3_rows_to_bf16(qb.numpy(), s.numpy())
+    nan = (ref & 0x7FFF) > 0x7F80
+    assert np.array_equal(nan, (got & 0x7FFF) > 0x7F80)
+    assert np.array_equal(got[~nan], ref[~nan])
+    assert np.array_equal(got[~nan], orc[~nan])
+
+
+@pytest.mark.parametrize("T", [1, 2, 17, 256])
+def test_fp8_linear_matches_reference(T):
+    """Lin.__call__ (qwen_engine.py:79-83) for T tokens.  T > 1: equal to the
+    reference's F.linear(x, (q.to(bf16) * s).to(bf16)) on the same device
+    (same bf16 weights, same GEMM), and within bf16 rounding of the oracle:
+    max |y - ref| <= 2^-7 max |ref|, and fewer than 1 % of the outputs differ
+    from the oracle's fp32 result rounded to bf16 (only accumulation order).
+    T == 1: the GEMV."""
+    N, K = 2560, 4096
+    q, s, _ = gemv_inputs(N, K, 11, 12)
+    x = torch.randn(T, K, generator=torch.Generator().manual_seed(T)).to(torch.bfloat16)
+    qd, sd, xd = cuda(q).view(torch.float8_e4m3fn), cuda(s)[:, None], x.to(DEV)
+    y = fp8gemv.linear(xd, qd, sd)
+    assert y.shape == (T, N) and y.dtype == torch.bfloat16
+    if T == 1:
+        assert torch.equal(y[0], fp8gemv.gemv(qd, sd.view(-1), xd[0]))
+        return
+    ref = torch.nn.functional.linear(xd, (qd.to(torch.bfloat16) * sd).to(torch.bfloat16))
+    assert torch.equal(y, ref)
+    got = y.float().cpu().numpy()
+    orc = oracle.fp8_linear(x.float().numpy(), q, s)
+    assert np.abs(got - orc).max() <= 2.0 ** -7 * np.abs(orc).max()
+    assert (got != oracle.bf16_round(orc)).mean() < 0.01

@@ -109,3 +109,20 @@ def test_prefill_oracle_matches_reference(golden):
     assert np.array_equal(coef, golden.load("prefill_t8_coef"))
     out = oracle.moe_prefill(x, ti, coef, table, 0, s2l)
     assert rel_err(out, golden.load("prefill_t8_out")) < 1e-5
+
+
+def test_e4m3_rows_to_bf16_matches_reference_expression():
+    """oracle.e4m3_rows_to_bf16 against qwen_engine.py:83 itself, executed by
+    torch on the CPU: (q.to(bf16) * s).to(bf16), every e4m3 byte, scales from
+    the engine's quantizer and extreme ones."""
+    g = np.random.default_rng(7)
+    q = np.tile(np.arange(256, dtype=np.uint8), (6, 4))                 # every byte, 6 rows x 1024
+    w = g.standard_normal((6, 1024)).astype(np.float32) * 0.02
+    s = np.concatenate([oracle.to_fp8_rows(w[:3])[1], np.float32([1e-12, 3.7e4, 0.3333333])])
+    ref = (torch.from_numpy(q).view(torch.float8_e4m3fn).to(torch.bfloat16)
+           * torch.from_numpy(s)[:, None]).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    got = oracle.e4m3_rows_to_bf16(q, s)
+    nan_ref = (ref & 0x7FFF) > 0x7F80
+    nan_got = (got & 0x7FFF) > 0x7F80
+    assert np.array_equal(nan_ref, nan_got)
+    assert np.array_equal(got[~nan_ref], ref[~nan_ref])            # incl. signed zeros and bf16 subnormals
