@@ -947,12 +947,15 @@ def main():
     h2d = d_x.numel() * 2 + d_sidx.numel() * 4 + d_s2.numel() * 4 + d_coef.numel() * 4
     d2h = L * HID * 4
 
+    # per-layer views of the step's input buffers (the caller's per-layer tensors)
+    per_layer = [(d_sidx[l], d_s2[l], d_coef[l], d_x[l]) for l in range(L)]
+
     def e2e_step(r):
         d_x.copy_(h_x[r], non_blocking=True)
         d_sidx.copy_(h_sidx[r], non_blocking=True)
         d_s2.copy_(h_s2[r], non_blocking=True)
         d_coef.copy_(h_coef[r], non_blocking=True)
-        outs = [qmoe.moe_decode(table.slots, d_sidx[l], d_s2[l], d_coef[l], d_x[l], hb, ob) for l in range(L)]
+        outs = [qmoe.moe_decode(table.slots, si, s2l, cl, xl, hb, ob) for si, s2l, cl, xl in per_layer]
         h_out[r].copy_(torch.stack(outs), non_blocking=True)
 
     for r in range(min(3, E)):

@@ -4,6 +4,7 @@ The library is loaded from this directory (built in-tree by build.py).  There
 is no fallback: if the library is missing or the device is not an sm_100
 part, every call raises.
 """
+import contextlib
 import ctypes
 import os
 
@@ -86,7 +87,18 @@ def prefill_status(clear=True):
 
 def stream_of(t):
     """Raw cudaStream_t of torch's current stream on tensor t's device."""
-    return torch.cuda.current_stream(t.device).cuda_stream
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
+
+
+_SAME_DEVICE = contextlib.nullcontext()
+
+
+def on_device(dev):
+    """Make `dev` the current CUDA device for a library call (the library
+    launches on the current device); free when it already is."""
+    if dev.index == torch._C._cuda_getDevice():
+        return _SAME_DEVICE
+    return torch.cuda.device(dev)
 
 
 def require_cuda(name, t, dtype=None, contiguous=True):

@@ -16,7 +16,7 @@ and the same bf16 GEMM.
 import torch
 import torch.nn.functional as F
 
-from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, stream_of
+from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, on_device, stream_of
 
 
 def _gemv(q, s, x, out_dtype):
@@ -31,7 +31,7 @@ def _gemv(q, s, x, out_dtype):
     if s.numel() != N or x.numel() != K:
         raise ValueError(f"s must have {N} and x {K} elements; got {s.numel()}, {x.numel()}")
     y = torch.empty(N, dtype=out_dtype, device=q.device)
-    with torch.cuda.device(q.device):
+    with on_device(q.device):
         rc = lib().qfn_gemv_e4m3(q.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(),
                                  DTYPE_F32 if out_dtype == torch.float32 else DTYPE_BF16, N, K, stream_of(y))
     check(rc, "qfn_gemv_e4m3")
@@ -66,7 +66,7 @@ def dequant_bf16(q, s):
     q = q.contiguous()
     s = s.reshape(-1).contiguous()
     w = torch.empty(N, K, dtype=torch.bfloat16, device=q.device)
-    with torch.cuda.device(q.device):
+    with on_device(q.device):
         rc = lib().qfn_e4m3_rows_to_bf16(q.data_ptr(), s.data_ptr(), w.data_ptr(), N, K, stream_of(w))
     check(rc, "qfn_e4m3_rows_to_bf16")
     return w

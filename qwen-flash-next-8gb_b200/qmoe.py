@@ -13,7 +13,7 @@ import ctypes
 
 import torch
 
-from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, stream_of
+from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, on_device, stream_of
 
 HID, INTER = 2560, 640
 BLOCK = 2764800
@@ -68,11 +68,12 @@ def _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant):
     if h_buf.dim() != 2 or h_buf.shape[0] < K or h_buf.shape[1] != INTER:
         raise ValueError(f"h_buf must be f32[>=K, {INTER}]")
     dev = slots_u8.device
+    di = slots_u8.get_device()
     for name, t in (("sidx", sidx), ("s2", s2), ("coef", coef), ("x", x), ("h_buf", h_buf)):
-        if t.device != dev:
+        if t.get_device() != di:
             raise ValueError(f"{name} is on {t.device}, slots_u8 on {dev}")
     out = torch.empty(HID, dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = lib().qfn_moe_decode_variant(slots_u8.data_ptr(), slots_u8.shape[0], sidx.data_ptr(),
                                           s2.data_ptr(), coef.data_ptr(), x.data_ptr(),
                                           DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16,
@@ -122,7 +123,7 @@ def moe_prefill(x, ti, tv, table, s2, L=0):
     L_ = lib()
     nbytes = L_.qfn_moe_prefill_workspace(T, topk, E)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = L_.qfn_moe_prefill(x.data_ptr(), T, ti.data_ptr(), int(ti.dtype == torch.int64), tv.data_ptr(),
                                 DTYPE_BF16 if tv.dtype == torch.bfloat16 else DTYPE_F32, topk, table.data_ptr(),
                                 table.shape[0], int(L) * E, s2.data_ptr(), E, out.data_ptr(), ws.data_ptr(),
@@ -144,7 +145,7 @@ def deq(w_u8, s_e4m3_u8, ws2):
     if tuple(s_e4m3_u8.shape) != (N, K // 16):
         raise ValueError(f"s must be [{N}, {K // 16}], got {tuple(s_e4m3_u8.shape)}")
     out = torch.empty(N, K, dtype=torch.float32, device=w_u8.device)
-    with torch.cuda.device(w_u8.device):
+    with on_device(w_u8.device):
         rc = lib().qfn_deq(w_u8.data_ptr(), s_e4m3_u8.data_ptr(), float(ws2), out.data_ptr(), N, K,
                            stream_of(out))
     check(rc, "qfn_deq")
@@ -162,7 +163,7 @@ def block_deq(blk_u8, s2):
     u = torch.empty(INTER, HID, dtype=torch.float32, device=dev)
     d = torch.empty(HID, INTER, dtype=torch.float32, device=dev)
     s2c = (ctypes.c_float * 3)(*vals)
-    with torch.cuda.device(dev):
+    with on_device(dev):
         rc = lib().qfn_block_deq(blk_u8.data_ptr(), ctypes.addressof(s2c), g.data_ptr(), u.data_ptr(),
                                  d.data_ptr(), stream_of(g))
     check(rc, "qfn_block_deq")
