@@ -136,75 +136,93 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
 }
 
 // ---------------------------------------------------------------------------
-// 2. x rows in pair order as f16 * 2^e (one CTA of 320 threads per pair)
-
-__device__ __forceinline__ float pf_block_max(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float u = __shfl_xor_sync(0xffffffffu, v, o);
-    v = (isnan(u) || u > v) ? u : v;
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float m = red[0];
-  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = (isnan(red[w]) || red[w] > m) ? red[w] : m;
-  return m;
-}
+// 2. x rows in pair order as f16 * 2^e (one warp per pair)
 
 __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(320) pf_gather_x_kernel(const uint16_t* __restrict__ x, const int* __restrict__ hdr,
-                                                          const int* __restrict__ pair_tok, __half* x16,
-                                                          int* pair_ex) {
-  __shared__ float red[10];
-  const int p = blockIdx.x;
-  if (p >= hdr[1]) return;
-  const int t = pair_tok[p];
-  const uint4 r = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * kHid)[threadIdx.x];
-  float v[8];
-  v[0] = bf16_bits_to_f32(r.x & 0xffffu); v[1] = bf16_bits_to_f32(r.x >> 16);
-  v[2] = bf16_bits_to_f32(r.y & 0xffffu); v[3] = bf16_bits_to_f32(r.y >> 16);
-  v[4] = bf16_bits_to_f32(r.z & 0xffffu); v[5] = bf16_bits_to_f32(r.z >> 16);
-  v[6] = bf16_bits_to_f32(r.w & 0xffffu); v[7] = bf16_bits_to_f32(r.w >> 16);
+// One warp per pair (8 per CTA of 256): a lane loads 10 of the row's 320
+// 16-byte chunks, the row maximum of |x| (NaN wins, as the block version it
+// replaced) meets in a warp shuffle, and no block barrier is needed.
+constexpr int kPfRowWarps = 8;
+
+__device__ __forceinline__ float pf_warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = nanmax_f(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__global__ void __launch_bounds__(32 * kPfRowWarps) pf_gather_x_kernel(const uint16_t* __restrict__ x,
+                                                                      const int* __restrict__ hdr,
+                                                                      const int* __restrict__ pair_tok,
+                                                                      __half* x16, int* pair_ex) {
+  constexpr int kChunks = kHid / 8 / 32;  // 16-byte chunks per lane: 10
+  const int lane = threadIdx.x & 31;
+  const int p = blockIdx.x * kPfRowWarps + (threadIdx.x >> 5);
+  if (p >= hdr[1]) return;  // warp-uniform
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(pair_tok[p]) * kHid);
+  uint4 r[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) r[i] = src[lane + 32 * i];
   float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = fabsf(v[i]);
-    m = (isnan(a) || a > m) ? a : m;
+  for (int i = 0; i < kChunks; ++i) {
+    const uint32_t w[4] = {r[i].x, r[i].y, r[i].z, r[i].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      m = nanmax_f(m, fabsf(bf16_bits_to_f32(w[k] & 0xffffu)));
+      m = nanmax_f(m, fabsf(bf16_bits_to_f32(w[k] >> 16)));
+    }
   }
-  const int e = f16_prescale_exp(pf_block_max(m, red));
-  uint4 o;
-  o.x = pack_f16x2(pow2_mul(v[0], e), pow2_mul(v[1], e));
-  o.y = pack_f16x2(pow2_mul(v[2], e), pow2_mul(v[3], e));
-  o.z = pack_f16x2(pow2_mul(v[4], e), pow2_mul(v[5], e));
-  o.w = pack_f16x2(pow2_mul(v[6], e), pow2_mul(v[7], e));
-  reinterpret_cast<uint4*>(x16 + static_cast<int64_t>(p) * kHid)[threadIdx.x] = o;
-  if (threadIdx.x == 0) pair_ex[p] = e;
+  const int e = f16_prescale_exp(pf_warp_max(m));
+  uint4* dst = reinterpret_cast<uint4*>(x16 + static_cast<int64_t>(p) * kHid);
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const uint32_t w[4] = {r[i].x, r[i].y, r[i].z, r[i].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      o[k] = pack_f16x2(pow2_mul(bf16_bits_to_f32(w[k] & 0xffffu), e), pow2_mul(bf16_bits_to_f32(w[k] >> 16), e));
+    dst[lane + 32 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (lane == 0) pair_ex[p] = e;
 }
 
 // ---------------------------------------------------------------------------
-// 4. h rows -> f16 hi / lo with one power-of-two scale per pair (160 threads)
+// 4. h rows -> f16 hi / lo with one power-of-two scale per pair (one warp per pair)
 
-__global__ void __launch_bounds__(160) pf_hpack_kernel(const float* __restrict__ h32, const int* __restrict__ hdr,
-                                                       __half* hhi, __half* hlo, int* pair_eh) {
-  __shared__ float red[5];
-  const int p = blockIdx.x;
-  if (p >= hdr[1]) return;
-  const float4 v = reinterpret_cast<const float4*>(h32 + static_cast<int64_t>(p) * kInter)[threadIdx.x];
-  float m = nanmax_f(nanmax_f(fabsf(v.x), fabsf(v.y)), nanmax_f(fabsf(v.z), fabsf(v.w)));
-  const int e = f16_prescale_exp(pf_block_max(m, red));
-  __half h[4], l[4];
-  split_f16(pow2_mul(v.x, e), h[0], l[0]);
-  split_f16(pow2_mul(v.y, e), h[1], l[1]);
-  split_f16(pow2_mul(v.z, e), h[2], l[2]);
-  split_f16(pow2_mul(v.w, e), h[3], l[3]);
-  reinterpret_cast<uint2*>(hhi + static_cast<int64_t>(p) * kInter)[threadIdx.x] = *reinterpret_cast<const uint2*>(h);
-  reinterpret_cast<uint2*>(hlo + static_cast<int64_t>(p) * kInter)[threadIdx.x] = *reinterpret_cast<const uint2*>(l);
-  if (threadIdx.x == 0) pair_eh[p] = e;
+// One warp per pair (8 per CTA): a lane takes 5 of the row's 160 float4.
+__global__ void __launch_bounds__(32 * kPfRowWarps) pf_hpack_kernel(const float* __restrict__ h32,
+                                                                   const int* __restrict__ hdr, __half* hhi,
+                                                                   __half* hlo, int* pair_eh) {
+  constexpr int kChunks = kInter / 4 / 32;  // float4 per lane: 5
+  const int lane = threadIdx.x & 31;
+  const int p = blockIdx.x * kPfRowWarps + (threadIdx.x >> 5);
+  if (p >= hdr[1]) return;  // warp-uniform
+  const float4* src = reinterpret_cast<const float4*>(h32 + static_cast<int64_t>(p) * kInter);
+  float4 v[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) v[i] = src[lane + 32 * i];
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i)
+    m = nanmax_f(m, nanmax_f(nanmax_f(fabsf(v[i].x), fabsf(v[i].y)), nanmax_f(fabsf(v[i].z), fabsf(v[i].w))));
+  const int e = f16_prescale_exp(pf_warp_max(m));
+  uint2* dh = reinterpret_cast<uint2*>(hhi + static_cast<int64_t>(p) * kInter);
+  uint2* dl = reinterpret_cast<uint2*>(hlo + static_cast<int64_t>(p) * kInter);
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    __half h[4], l[4];
+    split_f16(pow2_mul(v[i].x, e), h[0], l[0]);
+    split_f16(pow2_mul(v[i].y, e), h[1], l[1]);
+    split_f16(pow2_mul(v[i].z, e), h[2], l[2]);
+    split_f16(pow2_mul(v[i].w, e), h[3], l[3]);
+    dh[lane + 32 * i] = *reinterpret_cast<const uint2*>(h);
+    dl[lane + 32 * i] = *reinterpret_cast<const uint2*>(l);
+  }
+  if (lane == 0) pair_eh[p] = e;
 }
 
 // ---------------------------------------------------------------------------
@@ -782,8 +800,9 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   }
   if ((rc = check_launch("pf_route"))) return rc;
   // 2. x rows in pair order
-  pf_gather_x_kernel<<<static_cast<unsigned>(P), 320, 0, st>>>(static_cast<const uint16_t*>(x), hdr, pair_tok, x16,
-                                                                pair_ex);
+  const unsigned row_ctas = static_cast<unsigned>((P + kPfRowWarps - 1) / kPfRowWarps);
+  pf_gather_x_kernel<<<row_ctas, 32 * kPfRowWarps, 0, st>>>(static_cast<const uint16_t*>(x), hdr, pair_tok, x16,
+                                                            pair_ex);
   if ((rc = check_launch("pf_gather_x"))) return rc;
 
   // tensor maps
@@ -833,7 +852,7 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   PfArgs a{hdr, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, table, base, s2l, h32, out};
   if ((rc = pf_launch_gemm<kGateUp>(gu_maps, a, dev, st))) return rc;
   // 4. h -> f16 hi/lo
-  pf_hpack_kernel<<<static_cast<unsigned>(P), 160, 0, st>>>(h32, hdr, hhi, hlo, pair_eh);
+  pf_hpack_kernel<<<row_ctas, 32 * kPfRowWarps, 0, st>>>(h32, hdr, hhi, hlo, pair_eh);
   if ((rc = check_launch("pf_hpack"))) return rc;
   // 5. out = 0, 6. down + combine
   cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * kHid * sizeof(float), st);
