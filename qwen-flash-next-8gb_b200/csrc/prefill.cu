@@ -7,9 +7,10 @@
 // with the weights of qmoe.block_deq (qmoe.py:93-111): e2m1 code x E4M3 block
 // scale (one per 16 k) x per-tensor ws2.
 //
-// Pipeline (one stream, six launches):
-//  1. pf_route: (token, slot) pairs grouped by expert (counting sort), and
-//     tiles of up to 128 pairs of one expert.
+// Pipeline (one stream, eight launches):
+//  1. pf_count / pf_plan / pf_scatter: (token, slot) pairs grouped by expert
+//     (a counting sort over 64 slices of the pairs), and tiles of up to 128
+//     pairs of one expert.
 //  2. pf_gather_x: the x row of every pair in pair order, as f16 scaled by a
 //     power of two per token (max |x| in [2^14, 2^15)): exact for bf16 x.
 //  3. pf_gemm<GATEUP>: per (tile, 128 features): D[128 rows][pairs] = A x B^T
@@ -83,38 +84,53 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total)
   return incl - v;
 }
 
-// One CTA of 1024 threads.  ti: [T][topk] expert ids (int32 or int64), tv:
-// [T][topk] routing weights (bf16 or f32).  Outputs (workspace): hdr[0] =
-// number of tiles, hdr[1] = number of valid pairs; offs[E + 1]; pair_tok[P],
-// pair_w[P] (grouped by expert); tile_e/tile_p0/tile_n.
-template <typename TI, bool kTvBf16>
-__global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ ti, const void* __restrict__ tv,
-                                                        int64_t T, int topk, int E, int* hdr, int* offs,
-                                                        int* tile_e, int* tile_p0, int* tile_n, int* pair_tok,
-                                                        float* pair_w) {
-  __shared__ int cnt[kPfMaxExperts], cur[kPfMaxExperts], tmp[32];
+// Three launches.  ti: [T][topk] expert ids (int32 or int64), tv: [T][topk]
+// routing weights (bf16 or f32).  Outputs (workspace): hdr[0] = number of
+// tiles, hdr[1] = number of valid pairs; offs[E + 1]; pair_tok[P], pair_w[P]
+// (grouped by expert: by slice, then in shared-atomic order within a slice);
+// tile_e/tile_p0/tile_n.  Scratch: hist/base [kPfRouteCtas][E].
+constexpr int kPfRouteCtas = 64;  // CTAs of the count and scatter passes, each a contiguous slice of the pairs
+
+// (a) per-slice expert counts
+template <typename TI>
+__global__ void __launch_bounds__(1024) pf_count_kernel(const TI* __restrict__ ti, int64_t P, int E, int* hist) {
+  __shared__ int cnt[kPfMaxExperts];
   const int tid = threadIdx.x;
-  const int64_t P = T * topk;
   for (int i = tid; i < E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
-  for (int64_t p = tid; p < P; p += blockDim.x) {
+  const int64_t p0 = P * blockIdx.x / gridDim.x, p1 = P * (blockIdx.x + 1) / gridDim.x;
+  for (int64_t p = p0 + tid; p < p1; p += blockDim.x) {
     const int64_t e = static_cast<int64_t>(ti[p]);
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     else if (e != -1) pf_flag(kPfStatusBadExpert);  // -1 marks a pair to skip (expert-parallel padding)
   }
   __syncthreads();
-  const int c = tid < E ? cnt[tid] : 0;
+  for (int i = tid; i < E; i += blockDim.x) hist[blockIdx.x * E + i] = cnt[i];
+}
+
+// (b) one CTA (thread = expert): offsets, tiles, and each slice's first slot per expert
+__global__ void __launch_bounds__(1024) pf_plan_kernel(const int* __restrict__ hist, int G, int E, int* hdr, int* offs,
+                                                       int* tile_e, int* tile_p0, int* tile_n, int* base) {
+  __shared__ int tmp[32];
+  const int tid = threadIdx.x;
+  int c = 0;
+  if (tid < E)
+    for (int g = 0; g < G; ++g) c += hist[g * E + tid];
   int np, nt;
   const int o = block_exclusive_scan(c, tmp, &np);
   const int ntile = (c + kPfRows - 1) / kPfRows;
   const int tb = block_exclusive_scan(ntile, tmp, &nt);
   if (tid < E) {
     offs[tid] = o;
-    cur[tid] = o;
     for (int k = 0; k < ntile; ++k) {
       tile_e[tb + k] = tid;
       tile_p0[tb + k] = o + k * kPfRows;
       tile_n[tb + k] = min(kPfRows, c - k * kPfRows);
+    }
+    int b = o;
+    for (int g = 0; g < G; ++g) {
+      base[g * E + tid] = b;
+      b += hist[g * E + tid];
     }
   }
   if (tid == 0) {
@@ -122,8 +138,19 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
     hdr[0] = nt;
     hdr[1] = np;
   }
+}
+
+// (c) per-slice scatter of the pairs to their slots
+template <typename TI, bool kTvBf16>
+__global__ void __launch_bounds__(1024) pf_scatter_kernel(const TI* __restrict__ ti, const void* __restrict__ tv,
+                                                          int64_t P, int topk, int E, const int* __restrict__ base,
+                                                          int* pair_tok, float* pair_w) {
+  __shared__ int cur[kPfMaxExperts];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < E; i += blockDim.x) cur[i] = base[blockIdx.x * E + i];
   __syncthreads();
-  for (int64_t p = tid; p < P; p += blockDim.x) {
+  const int64_t p0 = P * blockIdx.x / gridDim.x, p1 = P * (blockIdx.x + 1) / gridDim.x;
+  for (int64_t p = p0 + tid; p < p1; p += blockDim.x) {
     const int64_t e = static_cast<int64_t>(ti[p]);
     if (e < 0 || e >= E) continue;
     const int pos = atomicAdd(&cur[e], 1);
@@ -133,6 +160,19 @@ __global__ void __launch_bounds__(1024) pf_route_kernel(const TI* __restrict__ t
     else w = static_cast<const float*>(tv)[p];
     pair_w[pos] = w;
   }
+}
+
+template <typename TI>
+static int pf_route(const TI* ti, const void* tv, bool tv_bf16, int64_t P, int topk, int E, int* hist, int* base,
+                    int* hdr, int* offs, int* tile_e, int* tile_p0, int* tile_n, int* pair_tok, float* pair_w,
+                    cudaStream_t st) {
+  pf_count_kernel<TI><<<kPfRouteCtas, 1024, 0, st>>>(ti, P, E, hist);
+  pf_plan_kernel<<<1, 1024, 0, st>>>(hist, kPfRouteCtas, E, hdr, offs, tile_e, tile_p0, tile_n, base);
+  if (tv_bf16)
+    pf_scatter_kernel<TI, true><<<kPfRouteCtas, 1024, 0, st>>>(ti, tv, P, topk, E, base, pair_tok, pair_w);
+  else
+    pf_scatter_kernel<TI, false><<<kPfRouteCtas, 1024, 0, st>>>(ti, tv, P, topk, E, base, pair_tok, pair_w);
+  return check_launch("pf_route");
 }
 
 // ---------------------------------------------------------------------------
@@ -692,7 +732,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // host side
 
 struct PfWs {  // byte offsets in the workspace
-  size_t hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, pair_eh, x16, h32, hhi, hlo, total;
+  size_t hdr, offs, rhist, rbase, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, pair_eh, x16, h32, hhi, hlo, total;
 };
 
 static inline size_t pf_align(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -704,6 +744,8 @@ static PfWs pf_ws_map(int64_t T, int topk, int E) {
   size_t o = 0;
   w.hdr = o; o = pf_align(o + 16);
   w.offs = o; o = pf_align(o + 4 * (E + 1));
+  w.rhist = o; o = pf_align(o + 4 * static_cast<size_t>(kPfRouteCtas) * E);
+  w.rbase = o; o = pf_align(o + 4 * static_cast<size_t>(kPfRouteCtas) * E);
   w.tile_e = o; o = pf_align(o + 4 * NT);
   w.tile_p0 = o; o = pf_align(o + 4 * NT);
   w.tile_n = o; o = pf_align(o + 4 * NT);
@@ -783,22 +825,13 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   const int64_t P = T * topk;
 
   // 1. routing
-  if (ti_is_int64) {
-    if (tv_dtype == QFN_DTYPE_BF16)
-      pf_route_kernel<int64_t, true><<<1, 1024, 0, st>>>(static_cast<const int64_t*>(ti), tv, T, topk, n_experts,
-                                                         hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w);
-    else
-      pf_route_kernel<int64_t, false><<<1, 1024, 0, st>>>(static_cast<const int64_t*>(ti), tv, T, topk, n_experts,
-                                                          hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w);
-  } else {
-    if (tv_dtype == QFN_DTYPE_BF16)
-      pf_route_kernel<int32_t, true><<<1, 1024, 0, st>>>(static_cast<const int32_t*>(ti), tv, T, topk, n_experts,
-                                                         hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w);
-    else
-      pf_route_kernel<int32_t, false><<<1, 1024, 0, st>>>(static_cast<const int32_t*>(ti), tv, T, topk, n_experts,
-                                                          hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w);
-  }
-  if ((rc = check_launch("pf_route"))) return rc;
+  int* rhist = reinterpret_cast<int*>(ws + W.rhist);
+  int* rbase = reinterpret_cast<int*>(ws + W.rbase);
+  rc = ti_is_int64 ? pf_route(static_cast<const int64_t*>(ti), tv, tv_dtype == QFN_DTYPE_BF16, P, topk, n_experts,
+                              rhist, rbase, hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w, st)
+                   : pf_route(static_cast<const int32_t*>(ti), tv, tv_dtype == QFN_DTYPE_BF16, P, topk, n_experts,
+                              rhist, rbase, hdr, offs, tile_e, tile_p0, tile_n, pair_tok, pair_w, st);
+  if (rc) return rc;
   // 2. x rows in pair order
   const unsigned row_ctas = static_cast<unsigned>((P + kPfRowWarps - 1) / kPfRowWarps);
   pf_gather_x_kernel<<<row_ctas, 32 * kPfRowWarps, 0, st>>>(static_cast<const uint16_t*>(x), hdr, pair_tok, x16,
