@@ -201,8 +201,9 @@ int qfn_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* w, int64_t
  *   workspace: device scratch of qfn_moe_prefill_workspace(T, topk,
  *          n_experts) bytes, 256-byte aligned.
  *   1 <= topk <= QFN_MAX_TOPK, 1 <= n_experts <= 1024, base + n_experts <=
- *   n_blocks.  Six launches on `stream` (routing sort, activation gather,
- *   tcgen05 gate/up GEMM, h packing, zeroing of out, tcgen05 down GEMM).
+ *   n_blocks.  Eight launches on `stream` (routing sort in three passes,
+ *   activation gather, tcgen05 gate/up GEMM, h packing, zeroing of out,
+ *   tcgen05 down GEMM).
  *   The combine adds with fp32 atomics, so the summation order over a
  *   token's experts varies between calls (as index_add_ on CUDA).
  */
