@@ -153,3 +153,27 @@ def test_prefill_routing_on_device_end_to_end(table64):
     assert np.array_equal(ti.cpu().numpy(), ti_ref)
     ref = oracle.moe_prefill(x.float().numpy(), ti_ref, coef_ref, blocks, 0, s2l)
     assert rel_err(out, ref) <= PREFILL_GRADE
+
+
+def test_prefill_at_the_expert_limit():
+    """n_experts = 1024 (the limit): every thread of the routing plan owns an
+    expert.  400 pairs over 1,024 experts, one expert with 100 of them; only
+    the routed experts' blocks are filled (no other block is read)."""
+    E, T, topk = 1024, 100, 4
+    rng = np.random.Generator(np.random.PCG64(21))
+    ti = np.stack([np.concatenate([[E - 1], rng.choice(E - 1, topk - 1, replace=False)]) for _ in range(T)])
+    ti = ti.astype(np.int32)
+    coef = rng.random((T, topk)).astype(np.float32)
+    used = np.unique(ti)
+    blocks = synthetic.make_blocks(len(used), seed=22)
+    table = torch.empty(E, qmoe.BLOCK, dtype=torch.uint8, device=DEV)
+    table[cuda(used).long()] = cuda(blocks)
+    s2l = synthetic.make_s2(E, seed=23, spread=True)
+    x = synthetic.make_x(T * 2560, seed=24).view(T, 2560)
+    out = run(x, ti, coef, table, s2l)
+    ti_used = np.searchsorted(used, ti).astype(np.int32)
+    ref = oracle.moe_prefill(x.float().numpy(), ti_used, coef, blocks, 0, s2l[used])
+    assert rel_err(out, ref) <= PREFILL_GRADE
+    assert (np.argmax(out, axis=1) == np.argmax(ref, axis=1)).all()
+    del table
+    torch.cuda.empty_cache()
