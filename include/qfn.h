@@ -109,9 +109,8 @@ int qfn_block_deq(const uint8_t* blk, const float s2[3], float* gate, float* up,
  *   CTAs' partial outputs meet in out through fp32 atomic adds, so repeated
  *   calls agree to fp32 rounding of the summation order, not bit for bit).
  *   The library keeps a small per-device array of call counters for it
- *   (file-scope device memory, nothing allocated per call).  Otherwise K <=
- *   10 runs the stream path (bit-reproducible; a grid barrier between h and
- *   the down projection) and larger K the two-launch CUDA-core path.
+ *   (file-scope device memory, nothing allocated per call).  Otherwise the
+ *   two-launch CUDA-core path runs (bit-reproducible).
  */
 int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                    const float* s2, const float* coef, const void* x, int x_dtype,
@@ -120,11 +119,10 @@ int qfn_moe_decode(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
 /*
  * qfn_moe_decode_variant -- qfn_moe_decode with the kernel path chosen by the
  * caller (no counterpart in the reference; for tests and measurements):
- * variant 0 = automatic (slice path for K <= 10, else CUDA-core path),
- * 1 = tensor-core path (one cooperative persistent launch: tcgen05
- * block-scaled FP4 MMA for gate/up, mma.sync for down; K <= 10; weight block
- * scales must be positive), 2 = CUDA-core path (two launches), 3 = stream path
- * (K <= 10, bit-reproducible), 4 = slice path (K <= 10, out 16-byte aligned).
+ * variant 0 = automatic (as qfn_moe_decode), 2 = CUDA-core path (two
+ * launches, any K), 4 = slice path (K <= 10, a 148-SM-class device, out
+ * 16-byte aligned).  Variants 1 and 3 named earlier paths that were removed
+ * and return QFN_ERR_UNSUPPORTED.
  */
 int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                            const float* s2, const float* coef, const void* x, int x_dtype,
@@ -138,13 +136,16 @@ int qfn_moe_decode_variant(const uint8_t* table, int64_t n_blocks, const int32_t
  * allocator calls).  No counterpart in the reference.  It takes no h_buf:
  * the h scratch is a file-scope device array of QFN_MAX_TOPK x 640 floats
  * (80 KB) that every device loading the library holds until exit.  The
- * entry point calls no allocator.  Its first call on a device resolves the
- * array's device address (cudaGetSymbolAddress): make that first call before
- * any stream capture.  All calls on a device share the array, so calls that
- * overlap on the GPU (different streams, no ordering between them) race;
- * calls in one stream are safe.  h is fully rewritten by every call, so
- * nothing needs clearing.  1 <= K <= QFN_MAX_TOPK, otherwise
- * QFN_ERR_UNSUPPORTED.  Other arguments as for qfn_moe_decode.
+ * entry point calls no allocator.  Its first call on a device (and its first
+ * call after that device's primary context was reset and created again)
+ * resolves the array's device address (cudaGetSymbolAddress): make that
+ * first call before any stream capture.  All calls on a device share the
+ * array, so calls that overlap on the GPU (different streams, no ordering
+ * between them) race.  Calls in one stream are safe: every decode kernel
+ * waits for the previous kernel in the stream before it writes h.  h is
+ * fully rewritten by every call, so nothing needs clearing.
+ * 1 <= K <= QFN_MAX_TOPK, otherwise QFN_ERR_UNSUPPORTED.  Other arguments
+ * as for qfn_moe_decode.
  */
 int qfn_moe_decode_noalloc(const uint8_t* table, int64_t n_blocks, const int32_t* sidx,
                            const float* s2, const float* coef, const void* x, int x_dtype,

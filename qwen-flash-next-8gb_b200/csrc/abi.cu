@@ -87,54 +87,11 @@ namespace {
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-struct TmapEntry {
-  const void* table;
-  int64_t n_blocks;
-  int device;
-  CUtensorMap map;
-};
-constexpr int kTmapSlots = 32;
-TmapEntry g_tmaps[kTmapSlots];
-int g_tmap_count = 0, g_tmap_next = 0;
 std::mutex g_tmap_mu;
 EncodeTiledFn g_encode = nullptr;
 }  // namespace
 
 namespace qfn {
-
-int gate_rows_tensor_map(const void* table, int64_t n_blocks, int device, CUtensorMap* out) {
-  std::lock_guard<std::mutex> lk(g_tmap_mu);
-  for (int i = 0; i < g_tmap_count; ++i)
-    if (g_tmaps[i].table == table && g_tmaps[i].n_blocks == n_blocks && g_tmaps[i].device == device) {
-      *out = g_tmaps[i].map;
-      return QFN_OK;
-    }
-  if (!g_encode) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || !fn) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
-  }
-  const int64_t rows = n_blocks * 2160;  // 2,764,800 B per block = 2160 rows of 1280 B
-  if (rows > (int64_t(1) << 31)) return set_error(QFN_ERR_UNSUPPORTED, "table too large for a tensor map");
-  CUtensorMap m;
-  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), 10};
-  cuuint64_t strides[2] = {1280, 128};
-  cuuint32_t box[3] = {128, 8, 10};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(table), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(QFN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-  TmapEntry& slot = g_tmaps[g_tmap_count < kTmapSlots ? g_tmap_count++ : (g_tmap_next++ % kTmapSlots)];
-  slot.table = table;
-  slot.n_blocks = n_blocks;
-  slot.device = device;
-  slot.map = m;
-  *out = m;
-  return QFN_OK;
-}
 
 }  // namespace qfn
 

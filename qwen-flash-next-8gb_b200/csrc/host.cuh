@@ -42,13 +42,6 @@ int check_launch(const char* what);
 
 namespace qfn {
 
-// 3-D TMA tensor map over the gate/up rows of an expert table viewed as
-// [n_blocks*2160 rows][10 chunks][128 B] (row stride 1280 B, chunk stride
-// 128 B), box [8 rows][10 chunks][128 B], 128-byte swizzle: one box is an
-// 8-row group of a gate or up matrix laid out as ten 1-KB UMMA K-major
-// SWIZZLE_128B atoms.  Cached per (device, table, n_blocks).
-int gate_rows_tensor_map(const void* table, int64_t n_blocks, int device, CUtensorMap* out);
-
 // 2-D TMA tensor map over `rows` rows of `inner` elements (row stride in
 // bytes), box [box_rows][box_inner], cached per (device, all arguments).
 int tensor_map_2d(const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t rows,

@@ -89,41 +89,75 @@ class ExpertTable:
         return self.slots[self.row(L, e)].cpu()
 
     # ---- filling
-    def fill_synthetic(self, seed=0):
-        from synthetic import fill_blocks_gpu
-        fill_blocks_gpu(self.slots, seed)
+    def fill_synthetic(self, seed=0, experts=None):
+        """Synthetic blocks (config-0 distributions): row L * n_experts + i gets
+        the block of (L, experts[i]) (default: the first n_experts), seeded per
+        (layer, global expert) so that any process can regenerate it."""
+        from synthetic import fill_table_gpu
+        experts = list(range(self.n_experts)) if experts is None else list(experts)
+        fill_table_gpu(self.slots, self.n_layers, experts, seed)
         return self
 
-    def load(self, experts_bin, experts_scal=None, chunk_blocks=64):
-        """Copy a repacked experts.bin (repack_experts.py layout, block (L,e) at
-        byte (L*n_experts+e)*BLOCK) and experts_scal.npy f32[L,E,6] into HBM.
-        Reads go through two pinned staging buffers so the disk read of chunk
-        i+1 overlaps the host->device copy of chunk i."""
-        n = self.slots.shape[0]
-        need = n * BLOCK
+    def load(self, experts_bin, experts_scal=None, experts=None, file_experts=512, chunk_blocks=64):
+        """Copy blocks of a repacked experts.bin and the ws2 of experts_scal.npy into the table.
+
+        File layout (repack_experts.py:8-19): block (L, e) at byte
+        (L * file_experts + e) * BLOCK, file_experts = 512 (NE, :11); scalars
+        f32[L, file_experts, 6] with ws2 gate/up/down in [..., :3]
+        (repack_experts.py:20-21, read as store.s2 at qwen_engine.py:370).
+        `experts` lists the global expert ids this table holds, in table
+        order (an expert-parallel shard; default: the first n_experts), so
+        table row L * n_experts + i holds file block (L, experts[i]).  On a
+        CUDA table, runs of consecutive file blocks are read through two
+        pinned staging buffers: the disk read of one chunk overlaps the
+        host->device copy of the previous one."""
+        experts = list(range(self.n_experts)) if experts is None else [int(e) for e in experts]
+        if len(experts) != self.n_experts or min(experts) < 0 or max(experts) >= file_experts:
+            raise ValueError(f"experts must list {self.n_experts} ids in [0, {file_experts})")
+        need = self.n_layers * file_experts * BLOCK
         size = os.path.getsize(experts_bin)
         if size < need:
-            raise ValueError(f"{experts_bin} has {size} bytes, the table needs {need}")
-        stage = [torch.empty(chunk_blocks * BLOCK, dtype=torch.uint8).pin_memory() for _ in range(2)]
-        events = [None, None]
-        side = torch.cuda.Stream(self.dev)
+            raise ValueError(f"{experts_bin} has {size} bytes, {self.n_layers} layers of {file_experts} "
+                             f"experts need {need}")
+        # (table row, file block, count) runs of consecutive blocks, at most chunk_blocks long
+        runs = []
+        for L in range(self.n_layers):
+            i = 0
+            while i < self.n_experts:
+                j = i + 1
+                while j < self.n_experts and j - i < chunk_blocks and experts[j] == experts[j - 1] + 1:
+                    j += 1
+                runs.append((L * self.n_experts + i, L * file_experts + experts[i], j - i))
+                i = j
+        cuda = self.slots.is_cuda
+        if cuda:
+            stage = [torch.empty(chunk_blocks * BLOCK, dtype=torch.uint8).pin_memory() for _ in range(2)]
+            events = [None, None]
+            side = torch.cuda.Stream(self.dev)
         with open(experts_bin, "rb", buffering=0) as f:
-            for i, b0 in enumerate(range(0, n, chunk_blocks)):
-                b1 = min(n, b0 + chunk_blocks)
-                buf = stage[i % 2]
-                if events[i % 2] is not None:
-                    events[i % 2].synchronize()
-                view = memoryview(buf.numpy())[: (b1 - b0) * BLOCK]
-                got = f.readinto(view)
-                if got != (b1 - b0) * BLOCK:
-                    raise IOError(f"short read at block {b0}: {got}")
-                with torch.cuda.stream(side):
-                    self.slots[b0:b1].view(-1).copy_(buf[: (b1 - b0) * BLOCK], non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(side)
-                events[i % 2] = ev
-        side.synchronize()
+            for k, (row, fblk, n) in enumerate(runs):
+                f.seek(fblk * BLOCK)
+                if not cuda:
+                    view = memoryview(self.slots[row:row + n].numpy()).cast("B")
+                    got = f.readinto(view)
+                else:
+                    buf = stage[k % 2]
+                    if events[k % 2] is not None:
+                        events[k % 2].synchronize()
+                    got = f.readinto(memoryview(buf.numpy())[: n * BLOCK])
+                    with torch.cuda.stream(side):
+                        self.slots[row:row + n].view(-1).copy_(buf[: n * BLOCK], non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(side)
+                    events[k % 2] = ev
+                if got != n * BLOCK:
+                    raise IOError(f"short read at file block {fblk}: {got} of {n * BLOCK} bytes")
+        if cuda:
+            side.synchronize()
         if experts_scal is not None:
             scal = np.load(experts_scal)
-            self.s2.copy_(torch.from_numpy(np.ascontiguousarray(scal[: self.n_layers, : self.n_experts, :3])))
+            if scal.ndim != 3 or scal.shape[0] < self.n_layers or scal.shape[1] != file_experts or scal.shape[2] < 3:
+                raise ValueError(f"experts_scal must be f32[>={self.n_layers}, {file_experts}, 6], got {scal.shape}")
+            sel = np.ascontiguousarray(scal[: self.n_layers][:, experts, :3], dtype=np.float32)
+            self.s2.copy_(torch.from_numpy(sel))
         return self

@@ -45,7 +45,8 @@ def moe_decode(slots_u8, sidx, s2, coef, x, h_buf, out_buf):
     return _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, 0)
 
 
-VARIANT_AUTO, VARIANT_TENSOR_CORE, VARIANT_CUDA_CORE, VARIANT_STREAM, VARIANT_SLICE = 0, 1, 2, 3, 4
+# kernel paths of qfn_moe_decode_variant (1 and 3 were earlier paths, since removed)
+VARIANT_AUTO, VARIANT_CUDA_CORE, VARIANT_SLICE = 0, 2, 4
 
 
 def _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant):

@@ -105,3 +105,40 @@ def fill_blocks_gpu(table, seed, chunk=256):
         view[:, O_GS:] = torch.exp2(u).to(torch.float8_e4m3fn).view(torch.uint8)
         del u
     return table
+
+
+def block_seed(seed, layer, expert):
+    """Seed of the synthetic block of (layer, global expert id): every process
+    can regenerate any expert's bytes, whichever rank's table holds it."""
+    return (int(seed) * 1000003 + int(layer) * 4099 + int(expert)) % (2 ** 62)
+
+
+@torch.no_grad()
+def fill_block_gpu(dst, seed):
+    """Fill one CUDA u8[BLOCK] block with the make_blocks distributions from
+    its own seed (torch's CUDA generator: the same bytes on every device)."""
+    g = torch.Generator(device=dst.device)
+    g.manual_seed(seed)
+    dst[:O_GS] = torch.randint(0, 256, (O_GS,), dtype=torch.uint8, device=dst.device, generator=g)
+    u = torch.empty(BLOCK - O_GS, dtype=torch.float32, device=dst.device)
+    u.uniform_(-4.0, 2.0, generator=g)
+    dst[O_GS:] = torch.exp2(u).to(torch.float8_e4m3fn).view(torch.uint8)
+    return dst
+
+
+@torch.no_grad()
+def fill_table_gpu(table, n_layers, experts, seed):
+    """Fill a CUDA table u8[n_layers * len(experts), BLOCK]: row L * len(experts)
+    + i holds the block of (L, experts[i]), seeded by block_seed."""
+    n = len(experts)
+    for L in range(n_layers):
+        for i, e in enumerate(experts):
+            fill_block_gpu(table[L * n + i], block_seed(seed, L, e))
+    return table
+
+
+@torch.no_grad()
+def expert_block(layer, expert, seed, dev):
+    """The synthetic block of (layer, expert) as a new CUDA u8[BLOCK] tensor
+    (what fill_table_gpu wrote into whichever table holds it)."""
+    return fill_block_gpu(torch.empty(BLOCK, dtype=torch.uint8, device=dev), block_seed(seed, layer, expert))

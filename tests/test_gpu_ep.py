@@ -44,7 +44,7 @@ def _worker(rank, port, results, mode="a2a"):
     try:
         blocks, s2, x, ti, tv = _inputs()
         shard = ep.ExpertShard(E, WORLD, rank)
-        own = slice(shard.first, shard.first + shard.per_rank)
+        own = shard.experts
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
         fn = ep.moe_prefill_ep if mode == "a2a" else ep.moe_prefill_ep_ag
         out = fn(x[toks].to(dev), torch.from_numpy(ti[toks]).long().to(dev),
