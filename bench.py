@@ -1,25 +1,41 @@
-"""Benchmark of the bs=1 NVFP4 decode MoE stack.
+"""Benchmark of the quantized matrix-product path of qwen-flash-next-8gb on B200.
 
-Workload: all 48 x 512 NVFP4 expert blocks (63.3 GiB, config-0 shapes and
-scale distributions) resident in HBM; per decode step (one token) 48 layers,
-each routed top-10 of 512 by fp32 logits with Zipf(1.1) popularity (one
-popularity permutation per layer, fresh Gumbel noise per step); x ~ N(0,1)
-bf16 per layer.  A step = 48 calls of the fused decode expert layer.
-Every step streams 48 x 27.66 MB of distinct expert bytes (1.33 GB >> the
-126 MB L2), so no L2 flush is needed between steps.
+BASELINE metric: "bs1 MoE-layer us & HBM GB/s vs 8 TB/s; prefill tokens/s at
+1/2/4/8 B200".  The headline line, at every N, is the batched prefill of one
+NVFP4 MoE layer (config 3): 2,048 tokens per GPU of x ~ N(0,1) bf16, routed
+top-10 of 512 experts with Zipf(1.1) popularity (fp32 logits = log p[perm] +
+Gumbel noise, one popularity permutation shared by all ranks), through the
+grouped SwiGLU expert GEMM and the weighted combine (qmoe.moe_prefill).
 
-  value  : aggregate algorithmic HBM GB/s (bytes of the 48 layers / device
-           time), graph-replayed steps with inputs resident in HBM, max over ranks.
-  e2e    : same metric through the public API (qmoe.moe_decode per layer,
-           eager), each step copying its inputs host->device from pinned memory
-           and its 48 outputs device->host.
-  N > 1  : replicas (bs=1 decode does not shard): every rank holds its own
-           table and runs the same workload; scaling "weak".
+  N = 1  : one GPU holds the layer's 512 experts.
+  N > 1  : expert-parallel, weak scaling: 512 / N experts per rank, placed by
+           load (a histogram of routed calibration tokens, ep.ExpertShard),
+           each rank routes its own 2,048 tokens; NCCL all-gather of the
+           tokens, the grouped GEMM over the rank's experts, reduce-scatter of
+           the fp32 sums (ep.moe_prefill_ep_ag; --ep-mode a2a: all-to-all).
 
+  value  : tokens/s of the whole job (all ranks' tokens / max-over-ranks device
+           time per step), inputs resident in HBM; every step reads >= 1.4 GB
+           of distinct expert blocks at N = 1 (> 126 MB L2: no flush needed).
+  e2e    : the same metric through the public call (qmoe.moe_prefill, or the
+           ep.* exchange at N > 1) with x, ti, tv copied in from pinned host
+           memory and the fp32 result copied back inside the timed region.
+  parity : a seeded sample of every rank's tokens checked against the CPU
+           oracle (tests' checker) after the timed region; the run exits
+           non-zero when it fails.
+
+Sub-records in the same line (same process, same expert table): at N = 1 the
+bs=1 decode layer over the 48-layer stack (config 2, the first half of the
+BASELINE metric), the FP8 GEMV (config 1) and batched decode (config 4); at
+N > 1 batched decode expert-parallel (config 4).  Each carries its own
+roofline, e2e, parity and (N = 1) CPU baseline.
+
+`--workload decode|gemv|batch-decode|fp8-linear` prints one of those alone.
 `--impl reference` times the reference's CPU path (the C restatement in
 oracle/) on this host's cores on a bounded sample of the same workload.
 """
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -32,50 +48,69 @@ PKG = os.path.join(REPO, "qwen-flash-next-8gb_b200")
 sys.path.insert(0, PKG)
 
 HID, INTER, BLOCK = 2560, 640, 2764800
-TOPK, N_EXPERTS = 10, 512
+TOPK, N_EXPERTS, N_LAYERS = 10, 512, 48
+WS2 = 1.0 / 448.0
 # algorithmic bytes of one decode layer: 10 expert blocks + s2 + coef + x (bf16) + out (fp32)
 LAYER_BYTES = TOPK * BLOCK + TOPK * 12 + TOPK * 4 + HID * 2 + HID * 4
-METRIC = "bs1 decode MoE-layer HBM GB/s (48-layer stack, experts resident in HBM)"
-# DRAM bytes (read + written) per launch measured with ncu (profiles/*.md)
-TRAFFIC_DECODE_SLICE = 27.74e6          # moe_decode_slice, one layer (K = 10)
-TRAFFIC_PREFILL_GEMMS = 1.767e9         # pf_gemm<0> + pf_gemm<1>, one config-3 layer
-TRAFFIC_GEMV_RATIO = 10.55e6 / 10.509312e6   # gemv_stream_kernel DRAM bytes / algorithmic bytes
-UNIT = "GB/s"
+PF_FLOP_PER_PAIR = 2 * 3 * INTER * HID          # gate, up and down: 9,830,400 FLOP per (token, expert)
+# our kernel launches per call
+PF_LAUNCHES = 7        # routing count / plan / scatter, x gather, gate/up GEMM, h packing, down GEMM
+PF_METRIC = "prefill tokens/s (one NVFP4 MoE layer: 2048 tokens per GPU, top-10 of 512 experts, Zipf(1.1))"
+DECODE_METRIC = "bs1 decode MoE-layer HBM GB/s (48-layer stack, experts resident in HBM)"
+GEMV_METRIC = "FP8 E4M3 row-scaled GEMV HBM GB/s (12288x2560, bs=1, per call)"
+BD_METRIC = "batched-decode tokens/s (batch 64 per GPU, 48-layer NVFP4 MoE stack, top-10 of 512 uniform)"
+GEMV_SHAPES = ((12288, 2560), (2560, 4096))   # the DeltaNet projections of config 1 (N x K)
+GEMV_COPIES = 8                                # weight copies rotated per shape (8 x 31.5 MB > 2 x L2)
+GEMV_CALLS = 64                                # calls per graph replay (one step)
+LIN_COPIES = 4
+
+# DRAM bytes (read + written) per launch of the dominant kernel of each
+# record, from ncu captures of the same shapes (None: not captured).
+TRAFFIC = {
+    "decode": 27.74e6,              # moe_decode_slice, one layer (K = 10)
+    "prefill": 1.767e9,             # pf_gemm<0> + pf_gemm<1>, one config-3 layer
+    "gemv_ratio": 10.55e6 / 10.509312e6,   # gemv_stream_kernel DRAM bytes / algorithmic bytes
+}
+PARITY_TOL = 1e-3       # north_star: max |err| <= 1e-3 x RMS of the oracle's output
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=256)
-    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="qfn", choices=["qfn", "reference"])
-    p.add_argument("--n-layers", type=int, default=48, help="table layers (48 = full config 2)")
-    p.add_argument("--routes", type=int, default=256, help="distinct routed steps (cycled)")
-    p.add_argument("--e2e-steps", type=int, default=32)
-    p.add_argument("--cpu-layers", type=int, default=4, help="layers timed for the CPU baseline")
-    p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--workload", default="decode", choices=["decode", "prefill", "gemv", "batch-decode", "fp8-linear"],
-                   help="decode: config 2 (default, the headline line); prefill: config 3; gemv: config 1; "
-                        "batch-decode: config 4; fp8-linear: the FP8 linear layer for T > 1 tokens")
+    p.add_argument("--workload", default="prefill",
+                   choices=["prefill", "decode", "gemv", "batch-decode", "fp8-linear"],
+                   help="prefill: config 3, the headline (with sub-records); the others print one record alone")
+    p.add_argument("--no-sub", action="store_true", help="headline only, no sub-records")
+    p.add_argument("--sub-steps", type=int, default=64, help="timed steps of each sub-record")
+    p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per GPU per step (config 3: 2048)")
     p.add_argument("--batch", type=int, default=64, help="batch-decode: tokens per GPU per step (config 4: 64)")
-    p.add_argument("--ep-mode", default="auto", choices=["auto", "a2a", "ag"],
-                   help="expert-parallel exchange under torchrun: a2a = all-to-all of routed rows (host sync "
-                        "for split sizes), ag = all-gather + reduce-scatter (no host sync); auto = ag")
-    p.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per step (config 3: 2048)")
-    p.add_argument("--cpu-tokens", type=int, default=24, help="prefill: tokens timed for the CPU baseline")
-    p.add_argument("--variant", type=int, default=0,
-                   help="decode kernel path: 0 auto (slice path for K <= 10), 3 stream, 4 slice, 2 CUDA-core")
+    p.add_argument("--n-layers", type=int, default=N_LAYERS, help="decode / batch-decode layers (48 = full)")
+    p.add_argument("--routes", type=int, default=32, help="decode: distinct routed steps (cycled)")
+    p.add_argument("--e2e-steps", type=int, default=32)
+    p.add_argument("--ep-mode", default="ag", choices=["ag", "a2a"],
+                   help="expert-parallel exchange: ag = all-gather + reduce-scatter (no host sync), "
+                        "a2a = all-to-all of routed rows (host sync for split sizes)")
+    p.add_argument("--placement", default="lpt", choices=["lpt", "contiguous"],
+                   help="expert placement over ranks for prefill: load-aware (LPT) or contiguous ranges")
+    p.add_argument("--parity-tokens", type=int, default=16, help="tokens per rank checked against the oracle")
+    p.add_argument("--cpu-tokens", type=int, default=128, help="prefill tokens timed for the CPU baseline")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--variant", type=int, default=0, help="decode kernel path: 0 auto, 4 slice, 2 CUDA-core")
+    p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, kind) from MEASURED_PEAKS.json, else the pool's fallback."""
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             m = json.load(f)
-        return float(m["hbm_gbs"]), "measured"
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
 class ClockSampler:
@@ -133,175 +168,237 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-# ---------------------------------------------------------------- reference arm
-def run_reference(args, rank):
-    if rank != 0:
-        return
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
+# ---------------------------------------------------------------- run context
+class Ctx:
+    """Device, process group and the shared 48-layer expert table of one rank."""
+
+    def __init__(self, args):
+        import torch
+        self.args = args
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = None
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+            self.dist = dist
+        self._table48 = None
+        self.failed = []
+
+    def table48(self):
+        """All n_layers x 512 experts of the stack (63.3 GiB at 48 layers), config-0 blocks."""
+        if self._table48 is None:
+            from expert_table import ExpertTable
+            t = ExpertTable(K=TOPK, dev=self.dev, n_layers=self.args.n_layers, n_experts=N_EXPERTS)
+            t.fill_synthetic(seed=self.args.seed)
+            self._table48 = t
+        return self._table48
+
+    def barrier(self):
+        import torch
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(self, v):
+        import torch
+        if self.dist is None:
+            return v
+        t = torch.tensor([float(v)], device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def min_over_ranks(self, v):
+        return -self.max_over_ranks(-v)
+
+    def timed(self, fn, steps, warmup, clocks=False):
+        """Device time per step (ms) of fn(i): warm-up, barrier + sync, CUDA events on
+        the current stream around `steps` calls, sync, max over ranks."""
+        import torch
+        for i in range(max(warmup, 3)):
+            fn(i)
+        self.barrier()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(self.local) if clocks else None
+        if clk:
+            clk.__enter__()
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(st)
+        for i in range(steps):
+            fn(i)
+        e1.record(st)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        if clk:
+            clk.__exit__()
+        ms = self.max_over_ranks(e0.elapsed_time(e1) / steps)
+        return (ms, clk.summary()) if clocks else ms
+
+    def parity(self, errs, argmax_ok, n):
+        """Max-over-ranks parity summary; records a failure."""
+        err = self.max_over_ranks(max(errs) if errs else 0.0)
+        ok = self.min_over_ranks(1.0 if argmax_ok else 0.0) > 0.5
+        total = int(round(self.max_over_ranks(n))) * self.world
+        res = {"max_err_rms": err, "argmax_equal": ok, "tol": PARITY_TOL, "checked_rows": total,
+               "checker": "oracle/ C restatement of the reference path on sampled rows", "pass": err <= PARITY_TOL and ok}
+        return res
+
+
+def rel_err(a, ref):
     import numpy as np
+    a = np.asarray(a, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(a - ref)) / np.sqrt(np.mean(ref * ref)))
+
+
+def oracle_mod(threads):
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
     import oracle
-    import synthetic
-    cores = oracle.threads(os.cpu_count())
-    if args.workload == "gemv":
-        N, K = GEMV_SHAPES[0]
-        q, sc = oracle.to_fp8_rows(synthetic.gemv_weights(N, K, seed=args.seed).float().numpy())
-        x = synthetic.make_x(K, seed=args.seed).float().numpy()
-        for _ in range(args.warmup):
-            oracle.gemv(q, sc, x)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            oracle.gemv(q, sc, x)
-        dt = time.perf_counter() - t0
-        v = args.steps * gemv_bytes(N, K) / dt / 1e9
-        sample = f"one {N}x{K} GEMV per step, C oracle, {cores} OpenMP threads"
-        print(json.dumps({
-            "impl": "reference", "metric": GEMV_METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"fp8-gemv (config 1): {N}x{K} per call, bs=1", "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
-            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
-        return
-    blocks = synthetic.make_blocks(TOPK, seed=args.seed)
-    sidx = np.arange(TOPK, dtype=np.int32)
-    s2 = synthetic.make_s2(TOPK)
-    ti, coef = oracle.route(synthetic.zipf_logits(1, seed=args.seed))
-    x = synthetic.make_x(HID, seed=args.seed).float().numpy()
-    for _ in range(args.warmup):
-        oracle.moe_decode(blocks, sidx, s2, coef[0], x)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.moe_decode(blocks, sidx, s2, coef[0], x)
-    dt = time.perf_counter() - t0
-    v = args.steps * LAYER_BYTES / dt / 1e9
-    sample = f"one decode layer (10 synthetic expert blocks) per step, C oracle, {cores} OpenMP threads"
-    print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "decode-moe-48L (config 2), CPU sample: 1 layer per step",
-                   "parallelism": "cpu"},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+    oracle.threads(threads)
+    return oracle
 
 
-# ---------------------------------------------------------------- qfn arm
-def build_workload(args, dev):
-    import torch
-    import routing
-    from expert_table import ExpertTable
-    L = args.n_layers
-    table = ExpertTable(K=TOPK, dev=dev, n_layers=L, n_experts=N_EXPERTS)
-    table.fill_synthetic(seed=args.seed)
-    g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 1)
-    R = args.routes
-    # Zipf(1.1) popularity, one permutation per layer; Gumbel-top-10 per step
-    logp = -1.1 * torch.log(torch.arange(1, N_EXPERTS + 1, device=dev, dtype=torch.float64))
-    logp = (logp - torch.logsumexp(logp, 0)).float()
-    perm = torch.stack([torch.randperm(N_EXPERTS, device=dev, generator=g) for _ in range(L)])
-    u = torch.rand(R, L, N_EXPERTS, device=dev, generator=g).clamp_(1e-12, 1 - 1e-7)
-    logits = logp[perm][None] - torch.log(-torch.log(u))
-    ti, tv = routing.route(logits.view(R * L, N_EXPERTS), TOPK)
-    ti = ti.view(R, L, TOPK)
-    layer = torch.arange(L, device=dev).view(1, L, 1)
-    sidx = (ti + layer * N_EXPERTS).to(torch.int32).contiguous()
-    s2 = table.s2[layer.expand_as(ti), ti].contiguous()              # [R, L, K, 3]
-    coef = tv.view(R, L, TOPK).float().contiguous()
-    x = torch.randn(R, L, HID, device=dev, generator=g).to(torch.bfloat16)
-    return table, sidx, s2, coef, x
+def host_threads(ctx):
+    return max(1, (os.cpu_count() or 1) // max(1, ctx.world))
 
 
-# ---------------------------------------------------------------- prefill (config 3)
-PF_TOPK = 10
-PF_FLOP_PER_PAIR = 2 * 3 * INTER * HID          # gate, up and down: 9,830,400 FLOP per (token, expert)
-PF_METRIC = "prefill tokens/s (one NVFP4 MoE layer: top-10 of 512 experts, Zipf(1.1) popularity)"
+class OracleSlices:
+    """The reference's expert loop (qwen_engine.py:838-852) on the CPU, one balanced slice
+    of a layer at a time: the layer's experts are split into `n` slices of equal expert
+    count and near-equal pairs (the load-aware placement of ep.ExpertShard), and a slice
+    runs every pair routed to its experts (block dequant + fp32 GEMMs + index_add into
+    the tokens' rows).  A slice is ~1/n of the full batch's work at the full batch's
+    expert reuse, so tokens/s = T / (n x time per slice)."""
+
+    def __init__(self, oracle, x, ti, tv, block_fn, n=64):
+        import numpy as np
+        import ep
+        self.oracle, self.x, self.ti, self.tv, self.block_fn, self.n = oracle, x, ti, tv, block_fn, n
+        load = np.bincount(ti.ravel(), minlength=N_EXPERTS)
+        self.lists = ep.ExpertShard(N_EXPERTS, n, 0, load=load).lists
+        self.out = np.zeros((x.shape[0], HID), np.float32)
+
+    def blocks(self, i):
+        return [self.block_fn(e) for e in self.lists[i % self.n]]
+
+    def run(self, i):
+        import numpy as np
+        experts = np.asarray(self.lists[i % self.n])
+        t, k = np.nonzero(np.isin(self.ti, experts))
+        if len(t) == 0:
+            return
+        used = np.unique(self.ti[t, k])
+        y = self.oracle.moe_prefill(self.x[t], np.searchsorted(used, self.ti[t, k]).astype(np.int32)[:, None],
+                                    self.tv[t, k][:, None], np.stack([self.block_fn(int(e)) for e in used]), 0,
+                                    np.full((len(used), 3), WS2, np.float32))
+        np.add.at(self.out, t, y)
 
 
-def prefill_inputs(args, dev, R):
-    """R routed steps of config 3: x bf16 [T, 2560] ~ N(0,1); fp32 logits = log p[perm] + Gumbel with
-    p_r ~ r^-1.1 (one popularity permutation), top-10 + renormalised bf16 weights (the engine's router)."""
+# ---------------------------------------------------------------- routing inputs
+def zipf_routes(dev, seed, rank_seed, T, R):
+    """R steps of T tokens: fp32 logits = log p[perm] + Gumbel, p_r ~ r^-1.1 with one
+    popularity permutation (from `seed`, shared by every rank), the noise and x from
+    `rank_seed`; routed top-10 + renormalised bf16 weights (the engine's router)."""
     import torch
     import routing
     g = torch.Generator(device=dev)
-    g.manual_seed(args.seed + 7)
-    T = args.tokens
+    g.manual_seed(seed)
     logp = -1.1 * torch.log(torch.arange(1, N_EXPERTS + 1, device=dev, dtype=torch.float64))
     logp = (logp - torch.logsumexp(logp, 0)).float()
     perm = torch.randperm(N_EXPERTS, device=dev, generator=g)
+    lp = logp[perm][None]
+    g.manual_seed(rank_seed)
     xs, tis, tvs = [], [], []
     for _ in range(R):
         u = torch.rand(T, N_EXPERTS, device=dev, generator=g).clamp_(1e-12, 1 - 1e-7)
-        ti, tv = routing.route(logp[perm][None] - torch.log(-torch.log(u)), PF_TOPK)
+        ti, tv = routing.route(lp - torch.log(-torch.log(u)), TOPK)
         xs.append(torch.randn(T, HID, device=dev, generator=g).to(torch.bfloat16))
         tis.append(ti)
         tvs.append(tv)
     return xs, tis, tvs
 
 
-def run_prefill(args, rank, world):
+def prefill_parity(ctx, out, x, ti, tv, layer, n, seed):
+    """out rows of n seeded tokens against the oracle's expert loop (qwen_engine.py:835-852);
+    the blocks the tokens route to are regenerated from their (layer, expert) seeds."""
+    import numpy as np
+    import torch
+    import synthetic
+    oracle = oracle_mod(host_threads(ctx))
+    T = x.shape[0]
+    rng = np.random.Generator(np.random.PCG64(seed))
+    tok = np.sort(rng.choice(T, size=min(n, T), replace=False))
+    ti_s = ti[torch.from_numpy(tok).to(ti.device)].cpu().numpy()
+    used = np.unique(ti_s)
+    blocks = torch.stack([synthetic.expert_block(layer, int(e), ctx.args.seed, ctx.dev) for e in used]).cpu().numpy()
+    ref = oracle.moe_prefill(x[tok].float().cpu().numpy(), np.searchsorted(used, ti_s).astype(np.int32),
+                             tv[tok].float().cpu().numpy(), blocks, 0, np.full((len(used), 3), WS2, np.float32))
+    got = out[tok].cpu().numpy()
+    return rel_err(got, ref), bool((got.argmax(1) == ref.argmax(1)).all()), len(tok)
+
+
+# ---------------------------------------------------------------- prefill (config 3): the headline
+def prefill_record(ctx):
+    import numpy as np
     import torch
     import qmoe
     from expert_table import ExpertTable
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = shard = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
+    args, dev, world, rank = ctx.args, ctx.dev, ctx.world, ctx.rank
+    T, R = args.tokens, 4
+    shard = ep_fn = None
+    if world == 1:
+        table = ctx.table48()
+        s2 = table.s2[0]
+    else:
         import ep
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        shard = ep.ExpertShard(N_EXPERTS, world, rank)
-    # expert-parallel: this rank holds 512 / world experts of the layer (its shard)
-    e_local = N_EXPERTS // world
-    table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=e_local)
-    table.fill_synthetic(seed=args.seed + rank)
-    s2 = table.s2[0].contiguous()
-    R = 4
-    args.seed += 1000 * rank              # every rank routes its own tokens (same popularity permutation)
-    xs, tis, tvs = prefill_inputs(args, dev, R)
-    T = args.tokens
-    pairs = T * PF_TOPK
-    distinct = [int(torch.unique(t).numel()) for t in tis]
-    layer_bytes = [d * BLOCK + T * HID * 2 + T * HID * 4 for d in distinct]
+        load = None
+        if args.placement == "lpt":
+            # calibration: a histogram of 4,096 routed tokens of the same popularity (same on every rank)
+            _, cti, _ = zipf_routes(dev, args.seed + 7, args.seed + 99, 4096, 1)
+            load = torch.bincount(cti[0].view(-1), minlength=N_EXPERTS).cpu().numpy()
+        shard = ep.ExpertShard(N_EXPERTS, world, rank, load=load)
+        table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=shard.per_rank)
+        table.fill_synthetic(seed=args.seed, experts=shard.experts)
+        s2 = table.s2[0]
+        ep_fn = ep.moe_prefill_ep_ag if args.ep_mode == "ag" else ep.moe_prefill_ep
+    xs, tis, tvs = zipf_routes(dev, args.seed + 7, args.seed + 8 + 1000 * rank, T, R)
 
-    ep_fn = None
-    if shard is not None:
-        ep_fn = ep.moe_prefill_ep if args.ep_mode == "a2a" else ep.moe_prefill_ep_ag
-
-    def step(i):
+    def call(x, ti, tv):
         if shard is None:
-            return qmoe.moe_prefill(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0)
-        return ep_fn(xs[i % R], tis[i % R], tvs[i % R], table.slots, s2, 0, shard)
+            return qmoe.moe_prefill(x, ti, tv, table.slots, s2, 0)
+        return ep_fn(x, ti, tv, table.slots, s2, 0, shard)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
+    ms, clk = ctx.timed(lambda i: call(xs[i % R], tis[i % R], tvs[i % R]), args.steps, args.warmup, clocks=True)
 
-    for i in range(max(args.warmup, 3)):
-        step(i)
-    barrier()
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("timed")
-        e0.record(st)
-        for i in range(args.steps):
-            step(i)
-        e1.record(st)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    ms = e0.elapsed_time(e1) / args.steps
-    if dist is not None:
-        t_ = torch.tensor([ms], device=dev)
-        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        ms = float(t_.item())
+    # work per step on this rank: its experts' distinct blocks + activations in + fp32 out
+    if shard is None:
+        distinct = [int(torch.unique(t).numel()) for t in tis]
+        pairs_rank = [T * TOPK] * R
+        rows = T
+    else:
+        # all ranks' tokens pass through every rank's grouped GEMM (ag) -- count this rank's experts' pairs
+        mine = shard.maps(dev)[2]
+        all_ti = [torch.cat(ctx_all_gather(ctx, t)) for t in tis]
+        distinct = [int(torch.unique(t[mine[t] >= 0]).numel()) for t in all_ti]
+        pairs_rank = [int((mine[t] >= 0).sum()) for t in all_ti]
+        rows = world * T if args.ep_mode == "ag" else T
+    step_bytes = sum(d * BLOCK for d in distinct) / R + rows * HID * (2 + 4)
+    pairs = sum(pairs_rank) / R
     tok_s = world * T / (ms * 1e-3)
-    tflops = world * pairs * PF_FLOP_PER_PAIR / (ms * 1e-3) / 1e12
-    avg_bytes = sum(layer_bytes[i % R] for i in range(args.steps)) / args.steps
-    gbs = avg_bytes / (ms * 1e-3) / 1e9       # one rank's expert bytes (for world > 1: its shard's share)
+    tflops_rank = pairs * PF_FLOP_PER_PAIR / (ms * 1e-3) / 1e12
+    gbs_rank = step_bytes / (ms * 1e-3) / 1e9
+    hbm, tc, kind = peaks()
+
+    # parity: step 0's output for a sample of this rank's tokens
+    out0 = call(xs[0], tis[0], tvs[0])
+    torch.cuda.synchronize()
+    e, ok, n = prefill_parity(ctx, out0, xs[0], tis[0], tvs[0], 0, args.parity_tokens, 1000 + rank)
+    parity = ctx.parity([e], ok, n)
+    del out0
 
     # e2e: host buffers in (x, ti, tv) and the fp32 result out, every step
     h_x = [x.cpu().pin_memory() for x in xs]
@@ -316,120 +413,216 @@ def run_prefill(args, rank, world):
         d_x.copy_(h_x[i % R], non_blocking=True)
         d_ti.copy_(h_ti[i % R], non_blocking=True)
         d_tv.copy_(h_tv[i % R], non_blocking=True)
-        if shard is None:
-            y = qmoe.moe_prefill(d_x, d_ti, d_tv, table.slots, s2, 0)
-        else:
-            y = ep_fn(d_x, d_ti, d_tv, table.slots, s2, 0, shard)
-        h_out.copy_(y, non_blocking=True)
+        h_out.copy_(call(d_x, d_ti, d_tv), non_blocking=True)
 
     E = min(args.e2e_steps, args.steps)
-    for i in range(2):
-        e2e_step(i)
-    barrier()
-    e0.record(st)
-    for i in range(E):
-        e2e_step(i)
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / E
-    if dist is not None:
-        t_ = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t_.item())
+    ms_e2e = ctx.timed(e2e_step, E, 2)
 
-    tc_peak, tc_kind = tensor_peak()
-    line = {
+    rec = {
         "metric": PF_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, "
                                       "fp32 accumulate", "data": "synthetic",
-        "config": {"workload": f"prefill-moe-1L (config 3): {T} tokens per GPU, top-{PF_TOPK} of {N_EXPERTS}, "
-                               f"Zipf(1.1), {pairs} pairs per GPU, {sum(distinct) / R:.0f} distinct experts per step"
-                               f" routed from rank 0's tokens",
-                   "tflops": tflops, "hbm_gbs": gbs, "bytes_per_step": avg_bytes,
-                   "flop_per_step": pairs * PF_FLOP_PER_PAIR,
-                   "l2": "no flush: each step reads >= 1.4 GB of distinct expert blocks (> 126 MB L2)",
-                   "parallelism": (f"expert-parallel x{world} (NCCL "
-                                   + ("all-to-all dispatch/combine" if args.ep_mode == "a2a"
-                                      else "all-gather + reduce-scatter") + ")") if world > 1
-                   else "single GPU"},
+        "config": {"workload": f"prefill-moe-1L (config 3): {T} tokens per GPU, top-{TOPK} of {N_EXPERTS}, Zipf(1.1)",
+                   "pairs_per_gpu": T * TOPK, "distinct_experts_per_step_rank": sum(distinct) / R,
+                   "tflops_per_gpu": tflops_rank, "hbm_gbs_per_gpu": gbs_rank, "bytes_per_step_rank": step_bytes,
+                   "l2": f"no flush: each step reads {step_bytes / 1e9:.2f} GB per rank (the distinct expert "
+                         "blocks of its routing and the activations; > 126 MB L2)",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"expert-parallel x{world} ({'all-gather + reduce-scatter' if args.ep_mode == 'ag' else 'all-to-all'}"
+                   f" over NCCL, {args.placement} placement, {N_EXPERTS // world} experts per rank)"},
         "e2e": {"value": world * T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
-                "path": "qmoe.moe_prefill (public API) with pinned host inputs and output"},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s",
-                     "frac": tflops / tc_peak, "peak_kind": tc_kind,
-                     "hbm_frac": gbs / peaks()[0],
-                     # the two GEMMs' DRAM bytes per layer, profiles/pf_gemm_prefill-layer.md
-                     "traffic": TRAFFIC_PREFILL_GEMMS if world == 1 and args.tokens == 2048 else None,
-                     "kernel": "pf_gemm<gate/up> + pf_gemm<down> (+ routing, gather, h packing)"},
-        "gpu_launches": args.steps * 6,
-        "clocks": clk.summary(),
+                "path": ("qmoe.moe_prefill" if world == 1 else f"ep.{ep_fn.__name__}") +
+                        " (public API) with pinned host x, ti, tv in and the fp32 result out"},
+        "roofline": {"bound": "hbm", "achieved": gbs_rank, "peak": hbm, "unit": "GB/s", "frac": gbs_rank / hbm,
+                     "peak_kind": kind, "tensor_tflops": tflops_rank, "tensor_peak": tc,
+                     "tensor_frac": tflops_rank / tc,
+                     "traffic": TRAFFIC["prefill"] if world == 1 and T == 2048 else None,
+                     "kernel": "qfn_moe_prefill, one layer (7 launches; the time is the whole layer's)" +
+                               ("" if world == 1 else " + the NCCL exchange")},
+        "parity": parity,
+        "gpu_launches": args.steps * PF_LAUNCHES,
+        "clocks": clk,
     }
-    if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = prefill_cpu_baseline(args, table, s2, xs[0], tis[0], tvs[0])
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
+    if shard is not None:
+        mean_pairs = T * TOPK
+        rec["config"]["pairs_per_rank_max_over_mean"] = ctx.max_over_ranks(sum(pairs_rank) / R) / mean_pairs
+    if world == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = prefill_cpu_baseline(ctx, xs[0], tis[0], tvs[0])
+    if not parity["pass"]:
+        ctx.failed.append("prefill")
+    return rec
 
 
-def tensor_peak():
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            m = json.load(f)
-        return float(m["bf16_tflops"]), "measured (burst)"
-    except Exception:
-        return 1590.0, "fallback"
+def ctx_all_gather(ctx, t):
+    import torch
+    out = [torch.empty_like(t) for _ in range(ctx.world)]
+    ctx.dist.all_gather(out, t.contiguous())
+    return out
 
 
-def prefill_cpu_baseline(args, table, s2, x, ti, tv):
-    """The C oracle's restatement of the expert loop (qwen_engine.py:838-852) on this host's cores for
-    the first `cpu_tokens` tokens of step 0 (every expert those tokens route to)."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
+def prefill_cpu_baseline(ctx, x, ti, tv):
+    """The C oracle's restatement of the expert loop (qwen_engine.py:838-852) on this host's
+    cores: 8 of the 64 balanced expert slices of step 0 (each slice: all pairs of its
+    experts at the full batch's reuse), scaled to the whole layer."""
     import numpy as np
-    import oracle
-    cores = oracle.threads(os.cpu_count())
-    n = min(args.cpu_tokens, x.shape[0])
-    ti_n = ti[:n].cpu().numpy().astype(np.int32)
-    used = sorted(set(ti_n.ravel().tolist()))
-    remap = {e: i for i, e in enumerate(used)}
-    blocks = table.slots[used].cpu().numpy()
-    ti_local = np.vectorize(remap.get)(ti_n).astype(np.int32)
-    s2_local = s2[used].cpu().numpy()
-    xf = x[:n].float().cpu().numpy()
-    tvf = tv[:n].float().cpu().numpy()
+    cores = host_threads(ctx)
+    oracle = oracle_mod(cores)
+    table = ctx.table48()
+    cache = {}
+
+    def block(e):
+        if e not in cache:
+            cache[e] = table.slots[e].cpu().numpy()
+        return cache[e]
+
+    sl = OracleSlices(oracle, x.float().cpu().numpy(), ti.cpu().numpy(), tv.float().cpu().numpy(), block)
+    m = 8
+    for i in range(m):
+        sl.blocks(i)             # device -> host copies stay out of the timed region
     t0 = time.perf_counter()
-    oracle.moe_prefill(xf, ti_local, tvf, blocks, 0, s2_local)
-    dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{n} tokens of step 0 ({len(used)} experts: block dequant + fp32 GEMMs + index_add), "
-                      f"{dt:.1f} s"}
+    for i in range(m):
+        sl.run(i)
+    dt = (time.perf_counter() - t0) / m
+    T = x.shape[0]
+    return {"value": T / (sl.n * dt), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{m} of {sl.n} balanced expert slices of step 0 ({T} tokens, top-{TOPK}; each slice: "
+                      f"block dequant + fp32 GEMMs + index_add for every pair of its experts), "
+                      f"{dt:.2f} s per slice, scaled x{sl.n}"}
+
+
+# ---------------------------------------------------------------- bs=1 decode (config 2)
+def decode_record(ctx, steps):
+    import numpy as np
+    import torch
+    import qmoe
+    import routing
+    args, dev = ctx.args, ctx.dev
+    table = ctx.table48()
+    L, R = args.n_layers, args.routes
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 1)
+    # Zipf(1.1) popularity, one permutation per layer; Gumbel-top-10 per step
+    logp = -1.1 * torch.log(torch.arange(1, N_EXPERTS + 1, device=dev, dtype=torch.float64))
+    logp = (logp - torch.logsumexp(logp, 0)).float()
+    perm = torch.stack([torch.randperm(N_EXPERTS, device=dev, generator=g) for _ in range(L)])
+    u = torch.rand(R, L, N_EXPERTS, device=dev, generator=g).clamp_(1e-12, 1 - 1e-7)
+    ti, tv = routing.route((logp[perm][None] - torch.log(-torch.log(u))).view(R * L, N_EXPERTS), TOPK)
+    ti = ti.view(R, L, TOPK)
+    layer = torch.arange(L, device=dev).view(1, L, 1)
+    sidx = (ti + layer * N_EXPERTS).to(torch.int32).contiguous()
+    s2 = table.s2[layer.expand_as(ti), ti].contiguous()              # [R, L, K, 3]
+    coef = tv.view(R, L, TOPK).float().contiguous()
+    x = torch.randn(R, L, HID, device=dev, generator=g).to(torch.bfloat16)
+    hb = torch.empty(TOPK, INTER, device=dev)
+    ob = torch.empty(TOPK, HID, device=dev)
+
+    def layer_call(r, l, xl=None):
+        xl = x[r, l] if xl is None else xl
+        if args.variant:
+            return qmoe._moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], xl, hb, args.variant)
+        return qmoe.moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], xl, hb, ob)
+
+    def step_eager(r):
+        for l in range(L):
+            layer_call(r, l)
+
+    step_eager(0)
+    torch.cuda.synchronize()
+    pool = torch.cuda.graph_pool_handle()
+    graphs = []
+    for r in range(R):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, pool=pool):
+            step_eager(r)
+        graphs.append(gr)
+    ms, clk = ctx.timed(lambda i: graphs[i % R].replay(), steps, args.warmup, clocks=True)
+    us_layer = ms * 1e3 / L
+    step_bytes = L * LAYER_BYTES
+
+    # parity: two layers of route 0 against the oracle
+    oracle = oracle_mod(host_threads(ctx))
+    errs, ok = [], True
+    for l in (0, L - 1):
+        y = layer_call(0, l).cpu().numpy()
+        blocks = table.slots[sidx[0, l].long()].cpu().numpy()
+        ref = oracle.moe_decode(blocks, np.arange(TOPK, dtype=np.int32), s2[0, l].cpu().numpy(),
+                                coef[0, l].cpu().numpy(), x[0, l].float().cpu().numpy())
+        errs.append(rel_err(y, ref))
+        ok = ok and int(y.argmax()) == int(ref.argmax())
+    parity = ctx.parity(errs, ok, 2)
+
+    # e2e: public API, eager, host inputs copied in and outputs copied out every step
+    E = min(args.e2e_steps, R)
+    h_x = x[:E].cpu().pin_memory()
+    h_sidx, h_s2, h_coef = sidx[:E].cpu().pin_memory(), s2[:E].cpu().pin_memory(), coef[:E].cpu().pin_memory()
+    d_x, d_sidx, d_s2, d_coef = torch.empty_like(x[0]), torch.empty_like(sidx[0]), torch.empty_like(s2[0]), \
+        torch.empty_like(coef[0])
+    h_out = torch.empty(E, L, HID).pin_memory()
+    h2d = d_x.numel() * 2 + d_sidx.numel() * 4 + d_s2.numel() * 4 + d_coef.numel() * 4
+    per_layer = [(d_sidx[l], d_s2[l], d_coef[l], d_x[l]) for l in range(L)]
+
+    def e2e_step(i):
+        r = i % E
+        d_x.copy_(h_x[r], non_blocking=True)
+        d_sidx.copy_(h_sidx[r], non_blocking=True)
+        d_s2.copy_(h_s2[r], non_blocking=True)
+        d_coef.copy_(h_coef[r], non_blocking=True)
+        outs = [qmoe.moe_decode(table.slots, si, s2l, cl, xl, hb, ob) for si, s2l, cl, xl in per_layer]
+        h_out[r].copy_(torch.stack(outs), non_blocking=True)
+
+    ms_e2e = ctx.timed(e2e_step, E, 3)
+    hbm, _, kind = peaks()
+    achieved = LAYER_BYTES / (us_layer * 1e-6) / 1e9
+    rec = {
+        "metric": DECODE_METRIC, "value": ctx.world * step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+        "us_per_layer": us_layer, "ms_per_step": ms, "steps": steps, "higher_is_better": True,
+        "dtype": "nvfp4 weights (e2m1 + e4m3 scales), fp32 accumulate",
+        "config": {"workload": f"decode-moe-{L}L (config 2): bs=1, top-{TOPK} of {N_EXPERTS}, Zipf(1.1), "
+                               f"{L}x{N_EXPERTS} experts resident ({L * N_EXPERTS * BLOCK / 2**30:.1f} GiB); "
+                               f"a step = {L} layers in one CUDA graph",
+                   "routes": R, "layer_bytes": LAYER_BYTES,
+                   "l2": "no flush: each step streams 1.33 GB of distinct expert bytes (> 126 MB L2)"},
+        "e2e": {"value": E * step_bytes / (ms_e2e * E * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": L * HID * 4, "ms_per_step": ms_e2e, "path": "qmoe.moe_decode per layer (eager)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "frac_of_8tbs": achieved / 8000.0,
+                     "traffic": TRAFFIC["decode"] if args.variant in (0, 4) else None, "per_launch_bytes": LAYER_BYTES,
+                     "kernel": "moe_decode_slice (one launch per decode layer)" if args.variant in (0, 4)
+                     else "moe_gate_up_generic + moe_down_generic"},
+        "parity": parity,
+        "gpu_launches": steps * L * (2 if args.variant == 2 else 1),
+        "clocks": clk,
+    }
+    if ctx.world == 1 and not args.no_cpu_baseline:
+        n = 2
+        layers = [(table.slots[sidx[0, l].long()].cpu().numpy(), np.arange(TOPK, dtype=np.int32),
+                   s2[0, l].cpu().numpy(), coef[0, l].cpu().numpy(), x[0, l].float().cpu().numpy()) for l in range(n)]
+        t0 = time.perf_counter()
+        for a in layers:
+            oracle.moe_decode(*a)
+        dt = time.perf_counter() - t0
+        rec["cpu_baseline"] = {"value": n * LAYER_BYTES / dt / 1e9, "unit": "GB/s", "cores": host_threads(ctx),
+                               "kind": "port", "sample": f"{n} layers of routed step 0 (C oracle: dequantize + fp32 "
+                                                         f"SwiGLU + combine), {dt / n * 1e3:.1f} ms/layer"}
+    if not parity["pass"]:
+        ctx.failed.append("decode")
+    del graphs
+    return rec
 
 
 # ---------------------------------------------------------------- FP8 GEMV (config 1)
-GEMV_SHAPES = ((12288, 2560), (2560, 4096))   # the DeltaNet projections of config 1 (N x K)
-GEMV_COPIES = 8                                # weight copies rotated per shape (8 x 31.5 MB > 2 x L2)
-GEMV_CALLS = 64                                # calls per graph replay (one step)
-GEMV_METRIC = "FP8 E4M3 row-scaled GEMV HBM GB/s (12288x2560, bs=1, per call)"
-
-
 def gemv_bytes(N, K):
     return N * K + 4 * N + 2 * K + 2 * N       # weights + row scales + x (bf16) + y (bf16)
 
 
-def run_gemv(args, rank, world):
+def gemv_record(ctx, steps):
+    import numpy as np
     import torch
     import fp8gemv
     import synthetic
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    args, dev = ctx.args, ctx.dev
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed + 11)
     per_shape = {}
@@ -457,161 +650,107 @@ def run_gemv(args, rank, world):
         with torch.cuda.graph(gr):
             calls(*shape)
         graphs[shape] = gr
-    torch.cuda.synchronize()
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    us_call = {}
-    clk_summary = None
+    us_call, clk = {}, None
     for shape in GEMV_SHAPES:
-        for _ in range(max(args.warmup, 3)):
-            graphs[shape].replay()
-        barrier()
-        with ClockSampler(local) as clk:
-            e0.record(st)
-            for _ in range(args.steps):
-                graphs[shape].replay()
-            e1.record(st)
-            torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if dist is not None:
-            t_ = torch.tensor([ms], device=dev)
-            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-            ms = float(t_.item())
-        us_call[shape] = ms * 1e3 / (args.steps * GEMV_CALLS)
-        if shape == GEMV_SHAPES[0]:
-            clk_summary = clk.summary()
-            ms_main = ms
+        ms, c = ctx.timed(lambda i, s=shape: graphs[s].replay(), steps, args.warmup, clocks=True)
+        us_call[shape] = ms * 1e3 / GEMV_CALLS
+        clk = clk or c
     N0, K0 = GEMV_SHAPES[0]
     b0 = gemv_bytes(N0, K0)
-    value = world * b0 / (us_call[GEMV_SHAPES[0]] * 1e-6) / 1e9
+
+    # parity: one call of each shape (fp32 result before the bf16 rounding) against the oracle
+    oracle = oracle_mod(host_threads(ctx))
+    errs = []
+    for (N, K), (qs, ss, xs) in per_shape.items():
+        y = fp8gemv.gemv_f32(qs[0], ss[0], xs[0]).cpu().numpy()
+        ref = oracle.gemv(qs[0].view(torch.uint8).cpu().numpy(), ss[0].cpu().numpy(), xs[0].float().cpu().numpy())
+        errs.append(rel_err(y, ref))
+    parity = ctx.parity(errs, True, len(errs))
 
     # e2e: the public API per call, x copied in from pinned host memory, y copied back
     qs, ss, xs = per_shape[GEMV_SHAPES[0]]
     h_x = [x.cpu().pin_memory() for x in xs]
     h_y = torch.empty(N0, dtype=torch.bfloat16).pin_memory()
     d_x = torch.empty_like(xs[0])
-    E = 256
 
     def e2e_call(i):
         d_x.copy_(h_x[i % 4], non_blocking=True)
-        y = fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], d_x)
-        h_y.copy_(y, non_blocking=True)
+        h_y.copy_(fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], d_x), non_blocking=True)
 
-    for i in range(8):
-        e2e_call(i)
-    barrier()
-    e0.record(st)
-    for i in range(E):
-        e2e_call(i)
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1)
-    if dist is not None:
-        t_ = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t_.item())
-    e2e_value = world * E * b0 / (ms_e2e * 1e-3) / 1e9
-
-    peak, peak_kind = peaks()
+    ms_e2e = ctx.timed(e2e_call, 256, 8)
+    hbm, _, kind = peaks()
     achieved = b0 / (us_call[GEMV_SHAPES[0]] * 1e-6) / 1e9
-    line = {
-        "metric": GEMV_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms_main / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 weights, bf16 x, fp32 accumulate", "data": "synthetic",
+    rec = {
+        "metric": GEMV_METRIC, "value": ctx.world * achieved, "unit": "GB/s", "steps": steps,
+        "us_per_call": {f"{N}x{K}": us_call[(N, K)] for (N, K) in GEMV_SHAPES}, "higher_is_better": True,
+        "dtype": "e4m3 weights, bf16 x, fp32 accumulate",
         "config": {"workload": f"fp8-gemv (config 1): {N0}x{K0} per call, bs=1; a step = {GEMV_CALLS} calls in one "
                                f"CUDA graph over {GEMV_COPIES} rotated weight copies",
-                   "us_per_call": {f"{N}x{K}": us_call[(N, K)] for (N, K) in GEMV_SHAPES},
                    "gbs_per_shape": {f"{N}x{K}": gemv_bytes(N, K) / (us_call[(N, K)] * 1e-6) / 1e9
                                      for (N, K) in GEMV_SHAPES},
                    "bytes_per_call": {f"{N}x{K}": gemv_bytes(N, K) for (N, K) in GEMV_SHAPES},
                    "l2": f"no flush: {GEMV_COPIES} rotated weight copies per shape "
-                         f"({GEMV_COPIES * N0 * K0 / 1e6:.0f} MB > 2 x 126 MB L2)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": K0 * 2, "d2h_bytes_per_step": N0 * 2,
-                "steps": E, "us_per_call": ms_e2e * 1e3 / E,
+                         f"({GEMV_COPIES * N0 * K0 / 1e6:.0f} MB > 2 x 126 MB L2)"},
+        "e2e": {"value": ctx.world * b0 / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": K0 * 2,
+                "d2h_bytes_per_step": N0 * 2, "us_per_call": ms_e2e * 1e3,
                 "path": "fp8gemv.gemv (public API, eager) with x from pinned host memory and y copied back"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "kernel": "gemv_stream_kernel",
-                     # profiles/gemv_stream_fp8-gemv.md captured the 2560x4096 shape (10.55 MB per
-                     # launch for 10.51 MB algorithmic); scaled to this shape by its bytes
-                     "traffic": TRAFFIC_GEMV_RATIO * b0,
-                     "per_launch_bytes": b0},
-        "gpu_launches": args.steps * GEMV_CALLS,
-        "clocks": clk_summary,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "kernel": "gemv_stream_kernel",
+                     # the capture is of the 2560x4096 shape; scaled to this shape by its algorithmic bytes
+                     "traffic": TRAFFIC["gemv_ratio"] * b0, "per_launch_bytes": b0},
+        "parity": parity,
+        "gpu_launches": steps * GEMV_CALLS,
+        "clocks": clk,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sys.path.insert(0, os.path.join(REPO, "oracle"))
-        import oracle
-        cores = oracle.threads(os.cpu_count())
-        q = qs[0].view(torch.uint8).cpu().numpy()
-        sc = ss[0].cpu().numpy()
-        xf = xs[0].float().cpu().numpy()
-        oracle.gemv(q, sc, xf)
+    if ctx.world == 1 and not args.no_cpu_baseline:
+        q, sc, xf = qs[0].view(torch.uint8).cpu().numpy(), ss[0].cpu().numpy(), xs[0].float().cpu().numpy()
         n = 3
         t0 = time.perf_counter()
         for _ in range(n):
             oracle.gemv(q, sc, xf)
         dt = (time.perf_counter() - t0) / n
-        line["cpu_baseline"] = {"value": b0 / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-                                "sample": f"{n} calls of the {N0}x{K0} GEMV (C oracle: e4m3 decode, fp64 dot "
-                                          f"products), {dt * 1e3:.1f} ms/call"}
-    if dist is not None:
-        del graphs
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
+        rec["cpu_baseline"] = {"value": b0 / dt / 1e9, "unit": "GB/s", "cores": host_threads(ctx), "kind": "port",
+                               "sample": f"{n} calls of the {N0}x{K0} GEMV (C oracle: e4m3 decode, fp64 dot "
+                                         f"products), {dt * 1e3:.1f} ms/call"}
+    if not parity["pass"]:
+        ctx.failed.append("gemv")
+    del graphs
+    return rec
 
 
 # ---------------------------------------------------------------- batched decode (config 4)
-BD_METRIC = "batched-decode tokens/s (batch 64 per GPU, 48-layer NVFP4 MoE stack, top-10 of 512 uniform)"
-
-
-def run_batch_decode(args, rank, world):
-    """Config 4: a step = one decode step of `--batch` tokens per GPU through all
-    `--n-layers` MoE layers; router logits ~ N(0,1) (uniform popularity), top-10
-    of 512 per layer, x ~ N(0,1) bf16 per layer.  1 GPU: the grouped expert GEMM
-    (qmoe.moe_prefill) per layer on the full table, one CUDA graph per step.
-    N GPUs: expert-parallel (each rank holds 512/N experts of every layer, its
-    own --batch tokens; NCCL all-to-all dispatch and combine per layer)."""
+def batch_decode_record(ctx, steps):
+    """A step = one decode step of --batch tokens per GPU through all --n-layers MoE
+    layers; router logits ~ N(0,1) (uniform popularity), top-10 of 512 per layer.  1 GPU:
+    qmoe.moe_prefill per layer on the 48-layer table, one CUDA graph per step.  N GPUs:
+    expert-parallel (512 / N experts of every layer per rank, contiguous: the popularity
+    is uniform), NCCL all-gather + reduce-scatter per layer, eager."""
+    import numpy as np
     import torch
     import qmoe
     import routing
     from expert_table import ExpertTable
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = shard = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        import ep
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        shard = ep.ExpertShard(N_EXPERTS, world, rank)
+    args, dev, world, rank = ctx.args, ctx.dev, ctx.world, ctx.rank
     L, B = args.n_layers, args.batch
-    e_local = N_EXPERTS // world
-    table = ExpertTable(K=TOPK, dev=dev, n_layers=L, n_experts=e_local)
-    table.fill_synthetic(seed=args.seed + rank)
+    shard = None
+    if world == 1:
+        table = ctx.table48()
+    else:
+        import ep
+        shard = ep.ExpertShard(N_EXPERTS, world, rank)
+        table = ExpertTable(K=TOPK, dev=dev, n_layers=L, n_experts=shard.per_rank)
+        table.fill_synthetic(seed=args.seed, experts=shard.experts)
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed + 23 + 1000 * rank)
     R = 2
     xs = torch.randn(R, L, B, HID, device=dev, generator=g).to(torch.bfloat16)
     ti, tv = routing.route(torch.randn(R * L * B, N_EXPERTS, device=dev, generator=g), TOPK)
     ti, tv = ti.view(R, L, B, TOPK).contiguous(), tv.view(R, L, B, TOPK).contiguous()
-    distinct = [[int(torch.unique(ti[r, l]).numel()) for l in range(L)] for r in range(R)]
-
-    mode = "ag" if args.ep_mode == "auto" else args.ep_mode
 
     def layer(x, t, v, l):
         if shard is None:
             return qmoe.moe_prefill(x, t, v, table.slots, table.s2[l], l)
-        if mode == "ag":
+        if args.ep_mode == "ag":
             return ep.moe_prefill_ep_ag(x, t, v, table.slots, table.s2[l], l, shard)
         return ep.moe_prefill_ep(x, t, v, table.slots, table.s2[l], l, shard)
 
@@ -620,7 +759,7 @@ def run_batch_decode(args, rank, world):
             layer(xs[r, l], ti[r, l], tv[r, l], l)
 
     graphs = None
-    if shard is None:  # expert-parallel steps run eagerly (NCCL collectives are not captured)
+    if shard is None:   # expert-parallel steps run eagerly (their NCCL collectives are not captured)
         step(0)
         torch.cuda.synchronize()
         graphs = []
@@ -630,45 +769,43 @@ def run_batch_decode(args, rank, world):
                 step(r)
             graphs.append(gr)
 
-    def run(r):
+    def run(i):
         if graphs is not None:
-            graphs[r % R].replay()
+            graphs[i % R].replay()
         else:
-            step(r % R)
+            step(i % R)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for i in range(max(args.warmup, 3)):
-        run(i)
-    barrier()
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(st)
-        for i in range(args.steps):
-            run(i)
-        e1.record(st)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    if dist is not None:
-        t_ = torch.tensor([ms], device=dev)
-        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        ms = float(t_.item())
-    tok_s = world * B / (ms * 1e-3)
-    step_bytes = sum(sum(d) * BLOCK for d in distinct) / R + L * B * HID * (2 + 4)   # experts + x in + fp32 out
+    ms, clk = ctx.timed(run, steps, args.warmup, clocks=True)
+    if shard is None:
+        distinct = sum(int(torch.unique(ti[r, l]).numel()) for r in range(R) for l in range(L)) / R
+    else:
+        mine = shard.maps(dev)[2]
+        distinct = 0
+        for r in range(R):
+            for l in range(L):
+                a = torch.cat(ctx_all_gather(ctx, ti[r, l]))
+                distinct += int(torch.unique(a[mine[a] >= 0]).numel())
+        distinct /= R
+    rows = B * (world if (shard is not None and args.ep_mode == "ag") else 1)
+    step_bytes = distinct * BLOCK + L * rows * HID * (2 + 4)
     gbs = step_bytes / (ms * 1e-3) / 1e9
+
+    # parity: layer 0 and the last layer of step 0, a sample of this rank's tokens
+    errs, ok, n = [], True, 0
+    for l in (0, L - 1):
+        out = layer(xs[0, l], ti[0, l], tv[0, l], l)
+        torch.cuda.synchronize()
+        e, o, k = prefill_parity(ctx, out, xs[0, l], ti[0, l], tv[0, l], l, 8, 2000 + 10 * rank + l)
+        errs.append(e)
+        ok, n = ok and o, n + k
+    parity = ctx.parity(errs, ok, n)
 
     # e2e: per step every layer's x, ti, tv from pinned host memory and its fp32 output back
     h_x, h_ti, h_tv = xs[0].cpu().pin_memory(), ti[0].cpu().pin_memory(), tv[0].cpu().pin_memory()
     h_out = torch.empty(L, B, HID, dtype=torch.float32).pin_memory()
     d_x, d_ti, d_tv = torch.empty_like(xs[0]), torch.empty_like(ti[0]), torch.empty_like(tv[0])
-    h2d = d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2
-    d2h = L * B * HID * 4
 
-    def e2e_step():
+    def e2e_step(i):
         d_x.copy_(h_x, non_blocking=True)
         d_ti.copy_(h_ti, non_blocking=True)
         d_tv.copy_(h_tv, non_blocking=True)
@@ -676,93 +813,60 @@ def run_batch_decode(args, rank, world):
             h_out[l].copy_(layer(d_x[l], d_ti[l], d_tv[l], l), non_blocking=True)
 
     E = min(args.e2e_steps, 8)
-    e2e_step()
-    barrier()
-    e0.record(st)
-    for _ in range(E):
-        e2e_step()
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / E
-    if dist is not None:
-        t_ = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t_.item())
-
-    peak, peak_kind = peaks()
-    line = {
-        "metric": BD_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, "
-                                      "fp32 accumulate", "data": "synthetic",
+    ms_e2e = ctx.timed(e2e_step, E, 1)
+    hbm, _, kind = peaks()
+    rec = {
+        "metric": BD_METRIC, "value": world * B / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": steps, "higher_is_better": True,
+        "dtype": "f16 tensor-core products of nvfp4 weights (exact) and bf16 activations, fp32 accumulate",
         "config": {"workload": f"batch-decode (config 4): {B} tokens per GPU, {L} layers, top-{TOPK} of "
-                               f"{N_EXPERTS} uniform; {sum(map(sum, distinct)) / R / L:.0f} distinct experts per "
-                               f"layer per rank's tokens",
-                   "hbm_gbs": gbs, "bytes_per_step": step_bytes,
+                               f"{N_EXPERTS} uniform; {distinct / L:.0f} distinct experts per layer per rank",
+                   "hbm_gbs_per_gpu": gbs, "bytes_per_step_rank": step_bytes,
                    "l2": "no flush: each step reads ~48 GB of distinct expert blocks (>> 126 MB L2)",
-                   "parallelism": (f"expert-parallel x{world} (NCCL " +
-                                   ("all-gather + reduce-scatter" if mode == "ag" else "all-to-all dispatch/combine")
-                                   + ")") if world > 1
-                   else "single GPU"},
-        "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"expert-parallel x{world} (NCCL {'all-gather + reduce-scatter' if args.ep_mode == 'ag' else 'all-to-all'}, eager)"},
+        "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2,
+                "d2h_bytes_per_step": L * B * HID * 4, "ms_per_step": ms_e2e,
                 "path": "qmoe.moe_prefill per layer (public API, eager) with pinned host inputs and outputs"},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                     "peak_kind": peak_kind, "traffic": None,
-                     "kernel": "pf_gemm<gate/up> + pf_gemm<down> (+ routing, gather, h packing) per layer"},
-        "gpu_launches": args.steps * L * 6,
-        "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_kind": kind, "traffic": None,
+                     "kernel": "qfn_moe_prefill per layer (7 launches; the time is the whole step's)"},
+        "parity": parity,
+        "gpu_launches": steps * L * PF_LAUNCHES,
+        "clocks": clk,
     }
-    if not args.no_cpu_baseline and world == 1:
-        sys.path.insert(0, os.path.join(REPO, "oracle"))
-        import numpy as np
-        import oracle
-        cores = oracle.threads(os.cpu_count())
+    if world == 1 and not args.no_cpu_baseline:
+        import synthetic
+        oracle = oracle_mod(host_threads(ctx))
         n = min(8, B)
         t_l = ti[0, 0, :n].cpu().numpy()
         used = np.unique(t_l)
-        remap = {int(e): i for i, e in enumerate(used)}
-        ti_local = np.vectorize(lambda e: remap[int(e)])(t_l).astype(np.int32)
-        blocks = table.slots[torch.from_numpy(used).to(dev)].cpu().numpy()
-        s2_local = table.s2[0][torch.from_numpy(used).to(dev)].cpu().numpy()
+        blocks = table.slots[used.tolist()].cpu().numpy()
         t0 = time.perf_counter()
-        oracle.moe_prefill(xs[0, 0, :n].float().cpu().numpy(), ti_local, tv[0, 0, :n].float().cpu().numpy(),
-                           blocks, 0, s2_local)
+        oracle.moe_prefill(xs[0, 0, :n].float().cpu().numpy(), np.searchsorted(used, t_l).astype(np.int32),
+                           tv[0, 0, :n].float().cpu().numpy(), blocks, 0, np.full((len(used), 3), WS2, np.float32))
         dt = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": n / (dt * L), "unit": "tokens/s", "cores": cores, "kind": "port",
-                                "sample": f"{n} tokens of layer 0 ({len(used)} experts: block dequant + fp32 GEMMs "
-                                          f"+ index_add) in {dt:.1f} s, extrapolated x{L} layers"}
-    if dist is not None:
-        del graphs  # graphs holding NCCL calls go before the process group
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
+        rec["cpu_baseline"] = {"value": n / (dt * L), "unit": "tokens/s", "cores": host_threads(ctx), "kind": "port",
+                               "sample": f"{n} tokens of layer 0 ({len(used)} experts: block dequant + fp32 GEMMs "
+                                         f"+ index_add) in {dt:.1f} s, extrapolated x{L} layers"}
+    if not parity["pass"]:
+        ctx.failed.append("batch-decode")
+    del graphs
+    return rec
 
 
-LIN_COPIES = 4                                 # weight copies per shape, rotated (4 x 42 MB > 126 MB L2)
-
-
-def run_fp8_linear(args, rank, world):
-    """The engine's FP8 linear layer for T > 1 tokens (Lin.__call__,
-    qwen_engine.py:79-83): --tokens (2048) tokens through the config-1 shapes
-    (12288x2560 and 2560x4096); a step = one call per shape through
-    fp8gemv.linear (this library's e4m3 -> bf16 kernel + the bf16 GEMM).  Also
-    timed on the same stream: the e4m3 -> bf16 kernel alone (its HBM roofline)
-    and the reference's own torch expression F.linear(x, (q.to(bf16) * s).to(bf16)).
-    N GPUs: replicas."""
+# ---------------------------------------------------------------- FP8 linear layer for T > 1
+def fp8_linear_record(ctx, steps):
+    """The engine's FP8 linear layer for T > 1 tokens (Lin.__call__, qwen_engine.py:79-83):
+    --tokens tokens through the config-1 shapes; a step = one call per shape through
+    fp8gemv.linear.  Also timed: the e4m3 -> bf16 weight kernel alone (its HBM roofline)
+    and the reference's own torch expression F.linear(x, (q.to(bf16) * s).to(bf16))."""
     import torch
     import torch.nn.functional as F
     import fp8gemv
     import synthetic
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    args, dev = ctx.args, ctx.dev
     T = args.tokens
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed + 31)
@@ -789,36 +893,16 @@ def run_fp8_linear(args, rank, world):
             q, sc = qs[i % LIN_COPIES], ss[i % LIN_COPIES]
             F.linear(x, (q.to(torch.bfloat16) * sc).to(torch.bfloat16))
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    st = torch.cuda.current_stream()
-
-    def timed(fn, clk=None):
-        for i in range(max(args.warmup, 3)):
-            fn(i)
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for i in range(args.steps):
-            fn(i)
-        e1.record(st)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        if dist is not None:
-            t_ = torch.tensor([ms], device=dev)
-            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-            ms = float(t_.item())
-        return ms
-
-    with ClockSampler(local) as clk:
-        ms = timed(ours)
-    ms_deq = timed(deq_only)
-    ms_ref = timed(reference)
-
-    # e2e: the public call with x copied in from pinned host memory and y read back, every step
+    ms, clk = ctx.timed(ours, steps, args.warmup, clocks=True)
+    ms_deq = ctx.timed(deq_only, steps, args.warmup)
+    ms_ref = ctx.timed(reference, steps, args.warmup)
+    errs = []
+    for qs, ss, x in data.values():
+        a = fp8gemv.linear(x, qs[0], ss[0])
+        b = F.linear(x, (qs[0].to(torch.bfloat16) * ss[0]).to(torch.bfloat16))
+        errs.append(float((a.float() - b.float()).abs().max() / b.float().pow(2).mean().sqrt()))
+    parity = ctx.parity(errs, True, len(errs))
+    parity["checker"] = "the reference's torch expression on the same GPU"
     hx = {k: v[2].cpu().pin_memory() for k, v in data.items()}
     hy = {(N, K): torch.empty(T, N, dtype=torch.bfloat16).pin_memory() for (N, K) in GEMV_SHAPES}
     dx = {k: torch.empty_like(v[2]) for k, v in data.items()}
@@ -828,208 +912,147 @@ def run_fp8_linear(args, rank, world):
             dx[k].copy_(hx[k], non_blocking=True)
             hy[k].copy_(fp8gemv.linear(dx[k], qs[i % LIN_COPIES], ss[i % LIN_COPIES]), non_blocking=True)
 
-    ms_e2e = timed(e2e)
+    ms_e2e = ctx.timed(e2e, steps, args.warmup)
     flop = sum(2 * T * N * K for (N, K) in GEMV_SHAPES)
     deq_bytes = sum(3 * N * K + 4 * N for (N, K) in GEMV_SHAPES)
-    value = world * flop / (ms * 1e-3) / 1e12
-    hbm, hbm_kind = peaks()
+    hbm, _, kind = peaks()
     deq_gbs = deq_bytes / (ms_deq * 1e-3) / 1e9
-    if rank == 0:
-        print(json.dumps({
-            "metric": f"fp8 linear layer, T={T} tokens, TFLOP/s (config-1 weight shapes)", "value": value,
-            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3 weights -> bf16, bf16 GEMM, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": f"fp8-linear: {T} tokens x (12288x2560 + 2560x4096), bf16 out",
-                       "us_reference_expression_same_gpu": ms_ref * 1e3, "us_dequant_kernel": ms_deq * 1e3,
-                       "l2": f"no flush: {LIN_COPIES} rotated weight copies per shape (> 126 MB L2)",
-                       "parallelism": "single GPU" if world == 1 else f"{world} replicas"},
-            "e2e": {"value": world * flop / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": sum(T * K * 2 for (N, K) in GEMV_SHAPES),
-                    "d2h_bytes_per_step": sum(T * N * 2 for (N, K) in GEMV_SHAPES), "ms_per_step": ms_e2e,
-                    "path": "fp8gemv.linear (public API) with pinned host x in and y out"},
-            "roofline": {"bound": "hbm", "achieved": deq_gbs, "peak": hbm, "unit": "GB/s", "frac": deq_gbs / hbm,
-                         "peak_kind": hbm_kind, "traffic": None,
-                         "kernel": "e4m3_rows_to_bf16_kernel (3 B per weight); the GEMM is cuBLAS"},
-            "gpu_launches": args.steps * len(GEMV_SHAPES),
-            "clocks": clk.summary(),
-        }))
-    if dist is not None:
-        dist.destroy_process_group()
+    return {
+        "metric": f"fp8 linear layer, T={T} tokens, TFLOP/s (config-1 weight shapes)",
+        "value": ctx.world * flop / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": ctx.world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 weights -> bf16, bf16 GEMM, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"fp8-linear: {T} tokens x (12288x2560 + 2560x4096), bf16 out",
+                   "us_reference_expression_same_gpu": ms_ref * 1e3, "us_dequant_kernel": ms_deq * 1e3,
+                   "l2": f"no flush: {LIN_COPIES} rotated weight copies per shape (> 126 MB L2)",
+                   "parallelism": "single GPU" if ctx.world == 1 else f"{ctx.world} replicas"},
+        "e2e": {"value": ctx.world * flop / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": sum(T * K * 2 for (N, K) in GEMV_SHAPES),
+                "d2h_bytes_per_step": sum(T * N * 2 for (N, K) in GEMV_SHAPES), "ms_per_step": ms_e2e,
+                "path": "fp8gemv.linear (public API) with pinned host x in and y out"},
+        "roofline": {"bound": "hbm", "achieved": deq_gbs, "peak": hbm, "unit": "GB/s", "frac": deq_gbs / hbm,
+                     "peak_kind": kind, "traffic": None,
+                     "kernel": "e4m3_rows_to_bf16_kernel (3 B per weight); the GEMM is cuBLAS"},
+        "parity": parity,
+        "gpu_launches": steps * len(GEMV_SHAPES),
+        "clocks": clk,
+    }
 
 
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank):
+    """The reference's CPU path (C restatement in oracle/, all host cores) on a bounded sample
+    per step of the same workload; rank 0 alone runs it."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    import synthetic
+    oracle = oracle_mod(os.cpu_count() or 1)
+    cores = oracle.threads(0)
+    line = {"impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic"}
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            fn(args.warmup + i)
+        return time.perf_counter() - t0
+
+    if args.workload in ("prefill", "batch-decode"):
+        T = args.tokens if args.workload == "prefill" else args.batch
+        if args.workload == "prefill":
+            ti, tv = oracle.route(synthetic.zipf_logits(T, seed=args.seed + 7), TOPK)
+        else:
+            ti, tv = oracle.route(synthetic.normal_logits(T, seed=args.seed + 23), TOPK)
+        x = synthetic.make_x(T * HID, seed=args.seed + 8, dtype=torch.float32).view(T, HID).numpy()
+        cache = {}
+
+        def block(e):
+            if e not in cache:
+                cache[e] = synthetic.make_blocks(1, seed=synthetic.block_seed(args.seed, 0, e))[0]
+            return cache[e]
+
+        n_slices = 64 if args.workload == "prefill" else 8
+        sl = OracleSlices(oracle, x, ti, tv, block, n=n_slices)
+        for i in range(min(n_slices, args.steps + args.warmup)):   # block generation stays out of the timing
+            sl.blocks(i)
+        dt = timed(sl.run)
+        per_token_layers = 1 if args.workload == "prefill" else args.n_layers
+        v = T * args.steps / (n_slices * dt) / per_token_layers
+        line.update({"metric": PF_METRIC if args.workload == "prefill" else BD_METRIC, "value": v,
+                     "unit": "tokens/s", "ms_per_step": dt / args.steps * 1e3,
+                     "config": {"workload": f"{args.workload} (config {'3' if args.workload == 'prefill' else '4'}), "
+                                            f"CPU sample: one of {n_slices} balanced expert slices of a {T}-token "
+                                            "layer per step", "parallelism": "cpu"}})
+        sample = (f"a step = 1/{n_slices} of one layer of {T} tokens (the pairs of {N_EXPERTS // n_slices} experts: "
+                  f"block dequant + fp32 GEMMs + index_add), C oracle, {cores} OpenMP threads; tokens/s = "
+                  f"{T} / ({n_slices} x time per step)" +
+                  ("" if args.workload == "prefill" else f" / {args.n_layers} layers"))
+    elif args.workload == "gemv":
+        N, K = GEMV_SHAPES[0]
+        q, sc = oracle.to_fp8_rows(synthetic.gemv_weights(N, K, seed=args.seed).float().numpy())
+        x = synthetic.make_x(K, seed=args.seed).float().numpy()
+        dt = timed(lambda i: oracle.gemv(q, sc, x))
+        v = args.steps * gemv_bytes(N, K) / dt / 1e9
+        line.update({"metric": GEMV_METRIC, "value": v, "unit": "GB/s", "ms_per_step": dt / args.steps * 1e3,
+                     "config": {"workload": f"fp8-gemv (config 1): {N}x{K} per call, bs=1", "parallelism": "cpu"}})
+        sample = f"one {N}x{K} GEMV per step, C oracle, {cores} OpenMP threads"
+    else:  # decode
+        blocks = synthetic.make_blocks(TOPK, seed=args.seed)
+        sidx = np.arange(TOPK, dtype=np.int32)
+        s2 = synthetic.make_s2(TOPK)
+        _, coef = oracle.route(synthetic.zipf_logits(1, seed=args.seed))
+        x = synthetic.make_x(HID, seed=args.seed).float().numpy()
+        dt = timed(lambda i: oracle.moe_decode(blocks, sidx, s2, coef[0], x))
+        v = args.steps * LAYER_BYTES / dt / 1e9
+        line.update({"metric": DECODE_METRIC, "value": v, "unit": "GB/s", "ms_per_step": dt / args.steps * 1e3,
+                     "config": {"workload": "decode-moe-48L (config 2), CPU sample: 1 layer per step",
+                                "parallelism": "cpu"}})
+        sample = f"one decode layer (10 synthetic expert blocks) per step, C oracle, {cores} OpenMP threads"
+    line["cpu_baseline"] = {"value": line["value"], "unit": line["unit"], "cores": cores, "kind": "port",
+                            "sample": sample}
+    line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------- main
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    ctx = Ctx(args)
+    sub_steps = min(args.sub_steps, args.steps) if args.steps > 0 else args.sub_steps
     if args.workload == "prefill":
-        return run_prefill(args, rank, world)
-    if args.workload == "gemv":
-        return run_gemv(args, rank, world)
-    if args.workload == "batch-decode":
-        return run_batch_decode(args, rank, world)
-    if args.workload == "fp8-linear":
-        return run_fp8_linear(args, rank, world)
-
-    import torch
-    import qmoe
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    table, sidx, s2, coef, x = build_workload(args, dev)
-    L, R = args.n_layers, args.routes
-    hb = torch.empty(TOPK, INTER, device=dev)
-    ob = torch.empty(TOPK, HID, device=dev)
-
-    def step_eager(r, outs=None):
-        for l in range(L):
-            if args.variant:
-                y = qmoe._moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], x[r, l], hb, args.variant)
-            else:
-                y = qmoe.moe_decode(table.slots, sidx[r, l], s2[r, l], coef[r, l], x[r, l], hb, ob)
-            if outs is not None:
-                outs.append(y)
-
-    # one CUDA graph per routed step (one kernel per layer)
-    step_eager(0)
-    torch.cuda.synchronize()
-    pool = torch.cuda.graph_pool_handle()
-    graphs = []
-    for r in range(R):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, pool=pool):
-            step_eager(r)
-        graphs.append(gr)
-    torch.cuda.synchronize()
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for i in range(args.warmup):
-        graphs[i % R].replay()
-    barrier()
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("timed")
-        e0.record(st)
-        for i in range(args.steps):
-            graphs[(args.warmup + i) % R].replay()
-        e1.record(st)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    step_bytes = L * LAYER_BYTES
-    value = world * args.steps * step_bytes / (ms * 1e-3) / 1e9
-    us_layer = ms * 1e3 / (args.steps * L)
-
-    # e2e: public API, eager, host inputs copied in and outputs copied out every step
-    E = min(args.e2e_steps, R)
-    h_x = x[:E].cpu().pin_memory()
-    h_sidx, h_s2, h_coef = sidx[:E].cpu().pin_memory(), s2[:E].cpu().pin_memory(), coef[:E].cpu().pin_memory()
-    d_x, d_sidx = torch.empty_like(x[0]), torch.empty_like(sidx[0])
-    d_s2, d_coef = torch.empty_like(s2[0]), torch.empty_like(coef[0])
-    h_out = torch.empty(E, L, HID).pin_memory()
-    h2d = d_x.numel() * 2 + d_sidx.numel() * 4 + d_s2.numel() * 4 + d_coef.numel() * 4
-    d2h = L * HID * 4
-
-    # per-layer views of the step's input buffers (the caller's per-layer tensors)
-    per_layer = [(d_sidx[l], d_s2[l], d_coef[l], d_x[l]) for l in range(L)]
-
-    def e2e_step(r):
-        d_x.copy_(h_x[r], non_blocking=True)
-        d_sidx.copy_(h_sidx[r], non_blocking=True)
-        d_s2.copy_(h_s2[r], non_blocking=True)
-        d_coef.copy_(h_coef[r], non_blocking=True)
-        outs = [qmoe.moe_decode(table.slots, si, s2l, cl, xl, hb, ob) for si, s2l, cl, xl in per_layer]
-        h_out[r].copy_(torch.stack(outs), non_blocking=True)
-
-    for r in range(min(3, E)):
-        e2e_step(r)
-    barrier()
-    e0.record(st)
-    for r in range(E):
-        e2e_step(r)
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
-    e2e_value = world * E * step_bytes / (ms_e2e * 1e-3) / 1e9
-
-    peak, peak_kind = peaks()
-    achieved = LAYER_BYTES / (us_layer * 1e-6) / 1e9
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "nvfp4 weights (e2m1 + e4m3 scales), fp32 accumulate", "data": "synthetic",
-        "config": {"workload": f"decode-moe-{L}L (config 2): bs=1, top-{TOPK} of {N_EXPERTS}, Zipf(1.1), "
-                               f"{L}x{N_EXPERTS} experts resident ({L * N_EXPERTS * BLOCK / 2**30:.1f} GiB)",
-                   "routes": R, "layer_bytes": LAYER_BYTES, "us_per_layer": us_layer,
-                   "l2": "no flush: each step streams >1.3 GB of distinct expert bytes (> 126 MB L2)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": E, "ms_per_step": ms_e2e / E, "path": "qmoe.moe_decode (eager, public API)"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind,
-                     "kernel": {0: "moe_decode_slice", 4: "moe_decode_slice", 3: "moe_decode_stream",
-                                2: "moe_gate_up_generic + moe_down_generic", 1: "moe_decode_persistent"}
-                     .get(args.variant, "?") + " (one launch per decode layer)",
-                     # DRAM bytes read + written per launch in the ncu capture of
-                     # profiles/moe_decode_slice_decode-layer.md (same layer shape)
-                     "traffic": TRAFFIC_DECODE_SLICE if args.variant in (0, 4) else None,
-                     "per_launch_bytes": LAYER_BYTES},
-        "gpu_launches": args.steps * L,
-        "clocks": clk.summary(),
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, table, sidx, s2, coef, x)
-    if dist is not None:
-        del graphs
-        dist.barrier()
-        dist.destroy_process_group()
+        line = prefill_record(ctx)
+        if not args.no_sub:
+            subs = {}
+            if ctx.world == 1:
+                subs["decode_config2"] = decode_record(ctx, max(sub_steps, 4))
+                subs["gemv_config1"] = gemv_record(ctx, max(sub_steps, 4))
+            subs["batch_decode_config4"] = batch_decode_record(ctx, max(sub_steps // 4, 4))
+            line["sub"] = subs
+    else:
+        fn = {"decode": decode_record, "gemv": gemv_record, "batch-decode": batch_decode_record,
+              "fp8-linear": fp8_linear_record}[args.workload]
+        line = fn(ctx, args.steps)
+        line.setdefault("n_gpus", ctx.world)
+        line.setdefault("warmup", max(args.warmup, 3))
+        line.setdefault("scaling", "weak")
+        line.setdefault("vs_baseline", None)
+        line.setdefault("data", "synthetic")
+    if ctx.dist is not None:
+        ctx.dist.barrier()
+        ctx.dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line))
-
-
-def cpu_baseline(args, table, sidx, s2, coef, x):
-    """The C oracle on this host's cores, on the first layers of routed step 0
-    (the same expert bytes the GPU read)."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import numpy as np
-    import oracle
-    cores = oracle.threads(os.cpu_count())
-    n = min(args.cpu_layers, args.n_layers)
-    layers = []
-    for l in range(n):
-        rows = sidx[0, l].long()
-        blocks = table.slots[rows].cpu().numpy()
-        layers.append((blocks, np.arange(TOPK, dtype=np.int32), s2[0, l].cpu().numpy(), coef[0, l].cpu().numpy(),
-                       x[0, l].float().cpu().numpy()))
-    oracle.moe_decode(*layers[0])
-    t0 = time.perf_counter()
-    for a in layers:
-        oracle.moe_decode(*a)
-    dt = time.perf_counter() - t0
-    return {"value": n * LAYER_BYTES / dt / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} layers of routed step 0 (C oracle: dequantize + fp32 SwiGLU + combine), "
-                      f"{dt / n * 1e3:.1f} ms/layer"}
+    if ctx.failed:
+        if rank == 0:
+            print(f"parity FAILED: {ctx.failed}", file=sys.stderr)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

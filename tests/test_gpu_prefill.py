@@ -177,3 +177,66 @@ def test_prefill_at_the_expert_limit():
     assert (np.argmax(out, axis=1) == np.argmax(ref, axis=1)).all()
     del table
     torch.cuda.empty_cache()
+
+
+def _oracle_on_tokens(x, ti, tv, table, s2l, tokens):
+    """The oracle's expert loop on a subset of the tokens (rows are independent:
+    a token's output depends only on its own routing), reading only the
+    blocks those tokens route to."""
+    ti_s = ti[tokens]
+    used = np.unique(ti_s)
+    blocks = table[cuda(used).long()].cpu().numpy()
+    ti_local = np.searchsorted(used, ti_s).astype(np.int32)
+    return oracle.moe_prefill(x[tokens], ti_local, tv[tokens], blocks, 0, s2l[used])
+
+
+@pytest.fixture(scope="module")
+def table512():
+    """One layer of 512 experts (1.4 GB), the BASELINE config-0 block distributions."""
+    t = torch.empty(512, qmoe.BLOCK, dtype=torch.uint8, device=DEV)
+    synthetic.fill_table_gpu(t, 1, list(range(512)), seed=77)
+    yield t
+    del t
+    torch.cuda.empty_cache()
+
+
+def test_prefill_config3_full_size(table512):
+    """BASELINE config 3 exactly: 2,048 tokens, top-10 of 512 experts with
+    Zipf(1.1) popularity (~20,480 pairs; the hottest expert holds ~1,800 pairs
+    over 15 tiles of 128).  A seeded sample of 48 tokens -- 16 of them routed
+    to the hottest expert, spread over its pair list, and the last token --
+    is checked against the oracle."""
+    T = 2048
+    logits = synthetic.zipf_logits(T, seed=81)
+    ti_d, tv_d = routing.route(cuda(logits), 10)
+    ti, tv = ti_d.cpu().numpy().astype(np.int32), tv_d.float().cpu().numpy()
+    s2l = synthetic.make_s2(512, seed=82, spread=True)
+    x = synthetic.make_x(T * 2560, seed=83).view(T, 2560)
+    out = qmoe.moe_prefill(x.to(DEV), ti_d, tv_d, table512, cuda(s2l), 0)
+    torch.cuda.synchronize()
+    out = out.cpu().numpy()
+    counts = np.bincount(ti.ravel(), minlength=512)
+    hot = int(np.argmax(counts))
+    assert counts[hot] > 6 * 128                      # a multi-tile expert
+    hot_tokens = np.nonzero((ti == hot).any(1))[0]
+    rng = np.random.Generator(np.random.PCG64(84))
+    tokens = np.unique(np.concatenate([hot_tokens[np.linspace(0, len(hot_tokens) - 1, 16).astype(int)],
+                                       rng.choice(T, 31, replace=False), [T - 1]]))
+    ref = _oracle_on_tokens(x.float().numpy(), ti, tv, table512, s2l, tokens)
+    assert rel_err(out[tokens], ref) <= PREFILL_GRADE
+    assert (np.argmax(out[tokens], axis=1) == np.argmax(ref, axis=1)).all()
+    assert np.isfinite(out).all()
+
+
+def test_batch_decode_config4_layer(table512):
+    """BASELINE config 4, one layer: 64 tokens, top-10 of 512 with uniform
+    popularity (router logits ~ N(0,1)), every token checked."""
+    T = 64
+    logits = synthetic.normal_logits(T, seed=91)
+    ti, tv = oracle.route(logits, 10)
+    s2l = synthetic.make_s2(512, seed=92, spread=True)
+    x = synthetic.make_x(T * 2560, seed=93).view(T, 2560)
+    out = run(x, ti, tv, table512, s2l, tv_dtype=torch.bfloat16)
+    ref = _oracle_on_tokens(x.float().numpy(), ti, tv, table512, s2l, np.arange(T))
+    assert rel_err(out, ref) <= PREFILL_GRADE
+    assert (np.argmax(out, axis=1) == np.argmax(ref, axis=1)).all()
