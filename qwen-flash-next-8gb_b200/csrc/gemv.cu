@@ -131,7 +131,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_e4m3_kernel(const uint8_t* 
 constexpr int kGsThreads = 512;
 constexpr int kGsWarps = kGsThreads / 32;
 constexpr int kGsMaxTilesPerCta = 16;
-constexpr int kGsSmemBudget = 225 * 1024;
+#ifndef QFN_GEMV_SMEM_KB
+#define QFN_GEMV_SMEM_KB 225
+#endif
+constexpr int kGsSmemBudget = QFN_GEMV_SMEM_KB * 1024;
 
 struct GsLayout {
   int slots, ring, xs, xraw, red, bar, total;
@@ -191,15 +194,18 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     mbar_arrive_expect_tx(&full[i % S], bytes);
     bulk_g2s(sm + L.ring + (i % S) * 16 * K, q + row0 * K, bytes, &full[i % S]);
   };
-  // Inputs may come from the previous kernel in the stream: wait for it (the
-  // launch and the prologue above overlap its tail).
+  // The weights and row scales are parameters that no kernel of the engine
+  // writes (the precondition of this entry point): the first ring of weight
+  // tiles is requested before the dependency wait, so it streams during the
+  // previous kernel's tail.  x may come from the previous kernel in the
+  // stream: it is copied only after the wait.
+  if (threadIdx.x == 0)
+    for (int i = 0; i < nt && i < S; ++i) issue(i);
   pdl_wait();
   pdl_launch_dependents();
-  // x first (ordinary loads would queue behind the weight stream), then the tiles.
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(&full[8], 2 * K);
     bulk_g2s(sm + L.xraw, x, 2 * K, &full[8]);
-    for (int i = 0; i < nt && i < S; ++i) issue(i);
   }
 
   // x -> f16 hi/lo * 2^ex (thread u owns k = u, u + 512, ...)
