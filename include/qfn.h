@@ -161,12 +161,63 @@ int qfn_moe_decode_noalloc(const uint8_t* table, int64_t n_blocks, const int32_t
 int qfn_device_status(unsigned int* status, int clear);
 
 /*
+ * qfn_moe_route -- replaces the router of QwenEngine.moe
+ * (qwen_engine.py:803-806) and the decode-argument gathers that follow it
+ * (qwen_engine.py:821-825), with no host synchronisation:
+ *   logits[t][e] = bf16(sum_k x[t][k] * w_router[e][k])   (fp32 sums)
+ *   probs = softmax(logits[t]) in fp32; ti[t] = the topk experts of highest
+ *   probability (equal probabilities: lower id first); tv[t][j] =
+ *   bf16(probs[ti[t][j]] / sum_j' probs[ti[t][j']]).
+ *   x:        bf16[T][2560] device, 16-byte aligned (raw 16-bit words).
+ *   w_router: bf16[n_experts][2560] device, 16-byte aligned.
+ *   ti:       int32[T][topk] device (expert ids).   tv: bf16[T][topk] device.
+ *   logits:   bf16[T][n_experts] device (output; the select step reads it).
+ *   Optional outputs for the decode entry points (null to skip):
+ *   sidx = sidx_base + ti (sidx_base = layer * n_experts: rows of the
+ *   HBM-resident expert table); coef = tv as fp32; s2_out[t][j][3] =
+ *   s2_layer[ti[t][j]][0..2] (s2_layer f32[n_experts][3], required with s2_out).
+ *   1 <= T <= 4096, n_experts % 4 == 0 and <= 1024, 1 <= topk <= 32.
+ *   Two launches (logits, then selection as a programmatic dependent); the
+ *   router weights are read before the dependency wait, so nothing earlier
+ *   in the stream may write w_router while it runs.
+ */
+int qfn_moe_route(const uint16_t* x, const uint16_t* w_router, int64_t T, int n_experts, int topk,
+                  int64_t sidx_base, const float* s2_layer, int32_t* ti, uint16_t* tv, int32_t* sidx,
+                  float* coef, float* s2_out, uint16_t* logits, qfn_stream_t stream);
+
+/*
+ * qfn_shared_expert -- replaces the shared expert of QwenEngine.moe and its
+ * combine with the routed experts (qwen_engine.py:817-818, 829-831), bf16
+ * weights (the engine's Lin layers outside linear_attn are bf16):
+ *   sh  = sigmoid(x . w_sg) * (w_down . (silu(w_gate . x) * (w_up . x)))
+ *   out = bf16(y) + sh            (y = the routed experts' fp32 output), or
+ *   out = sh                      (y = NULL)
+ *   each step rounded to bf16 where the reference's bf16 tensors round it;
+ *   dot products accumulate in fp32.
+ *   x: bf16[T][2560] device; w_gate, w_up: bf16[inter][2560]; w_down:
+ *   bf16[2560][inter]; w_sg: bf16[2560] (the [1, 2560] gate row); all
+ *   16-byte aligned.  y: f32[T][2560] device or NULL.
+ *   h: bf16[T][inter] device scratch (holds silu(g) * u on return), 16-byte
+ *   aligned; gt: bf16[T] device scratch (the gate); out: bf16[T][2560].
+ *   inter % 256 == 0, 256 <= inter <= 4096; 1 <= T <= 4096.
+ *   Two launches (gate/up, then down as a programmatic dependent); both read
+ *   their weight rows before the dependency wait, so nothing earlier in the
+ *   stream may write the weights while they run.
+ */
+int qfn_shared_expert(const uint16_t* x, int64_t T, const uint16_t* w_gate, const uint16_t* w_up,
+                      const uint16_t* w_down, const uint16_t* w_sg, int inter, const float* y,
+                      uint16_t* h, uint16_t* gt, uint16_t* out, qfn_stream_t stream);
+
+/*
  * qfn_gemv_e4m3 -- replaces fp8gemv.gemv (fp8gemv.py:20-26).
  *   y[n] = s[n] * sum_k e4m3(q[n][k]) * x[k], fp32 accumulation.
  *   q: u8[N][K] (float8_e4m3fn bytes) device, 16-byte aligned, K % 16 == 0.
  *   s: f32[N] device; x: bf16[K] device (raw 16-bit words).
  *   y: [N] device, y_dtype QFN_DTYPE_BF16 (the reference's output, rounded to
  *      nearest even) or QFN_DTYPE_F32 (the unrounded accumulator * s).
+ *   q and s are parameters: the kernel starts reading q before it waits for
+ *   the previous kernel in the stream, so no earlier kernel of the stream may
+ *   still be writing them (x may be).
  */
 int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
                   int y_dtype, int64_t N, int64_t K, qfn_stream_t stream);

@@ -179,3 +179,37 @@ def fp8_linear(x, q, s):
     (the caller rounds to bf16; the GPU GEMM's accumulation order differs)."""
     w = (e4m3_rows_to_bf16(q, s).astype(np.uint32) << 16).view(np.float32)
     return _c(x, np.float32) @ w.T
+
+
+def router_logits(x, w):
+    """F.linear(x, Ld["router"]) of qwen_engine.py:803 in bf16: x [T, H], w [E, H]
+    (bf16 values as fp32) -> fp32 [T, E] holding the bf16 rounding of the exact
+    dot products (fp64 sums; the GPU's fp32 summation order can land one bf16
+    step away when a sum lies next to a rounding boundary)."""
+    return bf16_round((_c(x, np.float64) @ _c(w, np.float64).T).astype(np.float32))
+
+
+def _silu(v):
+    return (v / (np.float32(1.0) + np.exp(-v, dtype=np.float32))).astype(np.float32)
+
+
+def shared_expert(x, wg, wu, wd, wsg, y=None):
+    """The shared expert of qwen_engine.py:817-818 (and the combine of :829)
+    with bf16 tensors, every step rounded to bf16 where the reference's bf16
+    tensors round it; dot products exact (fp64) before their bf16 rounding.
+      g = bf16(x.Wg), u = bf16(x.Wu), a = bf16(silu(g)), h = bf16(a * u),
+      d = bf16(h.Wd), gt = bf16(sigmoid(bf16(x.wsg))), sh = bf16(gt * d),
+      out = bf16(bf16(y) + sh) if y is given, else sh.
+    All arguments hold bf16 values as fp32 (y: fp32)."""
+    x = _c(x, np.float64)
+    g = bf16_round((x @ _c(wg, np.float64).T).astype(np.float32))
+    u = bf16_round((x @ _c(wu, np.float64).T).astype(np.float32))
+    a = bf16_round(_silu(g))
+    h = bf16_round(a * u)
+    d = bf16_round((h.astype(np.float64) @ _c(wd, np.float64).T).astype(np.float32))
+    z = bf16_round((x @ _c(wsg, np.float64).reshape(-1, 1)).astype(np.float32))
+    gt = bf16_round((np.float32(1.0) / (np.float32(1.0) + np.exp(-z, dtype=np.float32))).astype(np.float32))
+    sh = bf16_round(gt * d)
+    if y is None:
+        return sh
+    return bf16_round(bf16_round(_c(y, np.float32)) + sh)

@@ -33,6 +33,8 @@ SIGNATURES = {
     "qfn_moe_prefill_workspace": [_I64, _I, _I],
     "qfn_moe_prefill": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P],
     "qfn_prefill_status": [_P, _I],
+    "qfn_moe_route": [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
+    "qfn_shared_expert": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
 }
 # entry points whose return value is not an int status
 RESTYPES = {"qfn_moe_prefill_workspace": ctypes.c_size_t}

@@ -82,6 +82,22 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert lib.qfn_e4m3_rows_to_bf16(fake, fake, fake, 0, 32, None) == 1
     assert lib.qfn_e4m3_rows_to_bf16(fake, fake, fake, 4, 24, None) == 4
     assert lib.qfn_e4m3_rows_to_bf16(odd, fake, fake, 4, 32, None) == 2
+    # fused router: nulls, n_experts % 4, topk range, s2_out without s2_layer, alignment
+    r = lambda x, T, E, k, s2l, s2o: lib.qfn_moe_route(x, fake, T, E, k, 0, s2l, fake, fake, None, None, s2o, fake,
+                                                         None)
+    assert r(None, 1, 512, 10, None, None) == 1
+    assert r(fake, 1, 510, 10, None, None) == 4
+    assert r(fake, 1, 2048, 10, None, None) == 4
+    assert r(fake, 1, 512, 33, None, None) == 4
+    assert r(fake, 0, 512, 10, None, None) == 4
+    assert r(fake, 1, 512, 10, None, fake) == 1
+    assert r(odd, 1, 512, 10, None, None) == 2
+    # shared expert: nulls, inter % 256 and range, alignment
+    sh = lambda x, I: lib.qfn_shared_expert(x, 1, fake, fake, fake, fake, I, None, fake, fake, fake, None)
+    assert sh(None, 512) == 1
+    assert sh(fake, 320) == 4
+    assert sh(fake, 8192) == 4
+    assert sh(odd, 512) == 2
 
 
 def test_python_wrappers_reject_cpu_tensors():

@@ -1,0 +1,136 @@
+"""GPU parity of the decode MoE block's prologue and epilogue:
+the fused router (routing.route_fused, the C ABI's qfn_moe_route), the bf16
+shared expert with the combine (moe_block.shared_expert, qfn_shared_expert)
+and the whole device-side block (moe_block.DecodeMoE) against the CPU oracle.
+
+Router: the logits are the bf16 rounding of fp32 dot products, so they may sit
+one bf16 step from the exact value (oracle.router_logits) when a sum lies next
+to a rounding boundary; the top-k and the bf16 weights computed from the
+kernel's logits must equal the oracle's router (oracle.route, the reference's
+softmax / topk / renormalisation) exactly, and the torch expression of the
+reference on the same logits.
+"""
+import numpy as np
+import pytest
+import torch
+
+import moe_block
+import oracle
+import qmoe
+import routing
+import synthetic
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).to(DEV)
+
+
+def router_case(T, E, seed, dup_rows=0):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = bf16(rng.standard_normal((T, 2560)))
+    w = rng.standard_normal((E, 2560)) * 0.02
+    if dup_rows:   # identical rows: equal logits, the tie goes to the lower expert id
+        w[E - dup_rows:] = w[:dup_rows]
+    return x, bf16(w)
+
+
+@pytest.mark.parametrize("T,E,topk,seed", [(1, 512, 10, 1), (7, 512, 10, 2), (64, 512, 10, 3), (3, 128, 4, 4),
+                                           (2, 1024, 32, 5)])
+def test_route_fused_matches_oracle(T, E, topk, seed):
+    x, w = router_case(T, E, seed)
+    s2_table = torch.from_numpy(synthetic.make_s2(3 * E, seed=seed, spread=True).reshape(3, E, 3)).to(DEV)
+    layer = 2
+    r = routing.route_fused(x, w, topk, layer, s2_table)
+    torch.cuda.synchronize()
+    logits = r["logits"].float().cpu().numpy()
+    exact = oracle.router_logits(x.float().cpu().numpy(), w.float().cpu().numpy())
+    steps = np.abs(logits.view(np.int32) - exact.view(np.int32))
+    assert steps.max() <= 1 and (steps > 0).mean() < 0.02
+    ti_ref, coef_ref = oracle.route(logits, topk)
+    ti = r["ti"].cpu().numpy()
+    assert np.array_equal(ti, ti_ref)
+    assert np.array_equal(r["tv"].float().cpu().numpy(), coef_ref)
+    ti_t, tv_t = routing.route(r["logits"], topk)       # the reference's torch expression on the same logits
+    assert np.array_equal(ti_t.cpu().numpy(), ti) and torch.equal(tv_t, r["tv"])
+    assert np.array_equal(r["sidx"].cpu().numpy(), ti + layer * E)
+    assert np.array_equal(r["coef"].cpu().numpy(), coef_ref)
+    assert torch.equal(r["s2"], s2_table[layer][r["ti"].long()])
+
+
+def test_route_fused_ties_go_to_the_lower_expert():
+    x, w = router_case(5, 512, 11, dup_rows=256)         # experts e and e + 256 have equal logits
+    r = routing.route_fused(x, w, 10)
+    logits = r["logits"].float().cpu().numpy()
+    ti_ref, coef_ref = oracle.route(logits, 10)
+    assert np.array_equal(r["ti"].cpu().numpy(), ti_ref)
+    assert np.array_equal(r["tv"].float().cpu().numpy(), coef_ref)
+    assert (r["ti"].cpu().numpy() < 256).all()
+
+
+def shared_case(T, I, seed):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = bf16(rng.standard_normal((T, 2560)))
+    wg, wu = bf16(rng.standard_normal((I, 2560)) * .02), bf16(rng.standard_normal((I, 2560)) * .02)
+    wd, wsg = bf16(rng.standard_normal((2560, I)) * .02), bf16(rng.standard_normal((1, 2560)) * .02)
+    y = torch.from_numpy(rng.standard_normal((T, 2560)).astype(np.float32)).to(DEV)
+    return x, wg, wu, wd, wsg, y
+
+
+@pytest.mark.parametrize("T,I,seed,with_y", [(1, 512, 1, True), (1, 512, 2, False), (9, 256, 3, True),
+                                             (4, 1536, 4, True), (2, 4096, 5, False)])
+def test_shared_expert_matches_oracle(T, I, seed, with_y):
+    """bf16 results equal the oracle's (each step rounded to bf16 as the
+    reference rounds it) but for rare one-step differences where an fp32 sum
+    lies next to a bf16 rounding boundary."""
+    x, wg, wu, wd, wsg, y = shared_case(T, I, seed)
+    out = moe_block.shared_expert(x, wg, wu, wd, wsg, y if with_y else None)
+    torch.cuda.synchronize()
+    ref = oracle.shared_expert(*(t.float().cpu().numpy() for t in (x, wg, wu, wd, wsg)),
+                               y.cpu().numpy() if with_y else None)
+    got = out.float().cpu().numpy()
+    steps = np.abs(got.view(np.int32) - ref.view(np.int32))
+    assert np.isfinite(got).all()
+    assert rel_err(got, ref) <= 1e-2      # a few bf16 steps at most, relative to RMS
+    assert (steps > 0).mean() < 0.02
+
+
+def test_decode_moe_block_device_only_in_a_graph():
+    """The decode MoE block (router -> routed experts -> shared expert + combine)
+    on the device, captured in one CUDA graph: replayed on new inputs it equals
+    the oracle's block on the same routing; nothing leaves the GPU."""
+    from expert_table import ExpertTable
+    E, L = 64, 2
+    table = ExpertTable(K=10, dev=DEV, n_layers=L, n_experts=E)
+    table.fill_synthetic(seed=3)
+    table.s2.copy_(torch.from_numpy(synthetic.make_s2(L * E, seed=4, spread=True).reshape(L, E, 3)))
+    _, router = router_case(1, E, 21)
+    _, wg, wu, wd, wsg, _ = shared_case(1, 512, 22)
+    blk = moe_block.DecodeMoE(table, topk=10)
+    x = bf16(synthetic.make_x(2560, seed=23).float().numpy()[None])
+    out = torch.empty(1, 2560, dtype=torch.bfloat16, device=DEV)
+    blk(x, 1, router, wg, wu, wd, wsg, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        blk(x, 1, router, wg, wu, wd, wsg, out=out)
+    x.copy_(bf16(synthetic.make_x(2560, seed=24).float().numpy()[None]))
+    g.replay()
+    torch.cuda.synchronize()
+    # the oracle's block on the kernel's routing (which the router test pins)
+    ti = blk.route_buf["ti"][0].cpu().numpy()
+    coef = blk.route_buf["tv"][0].float().cpu().numpy()
+    logits = blk.route_buf["logits"].float().cpu().numpy()
+    ti_ref, coef_ref = oracle.route(logits, 10)
+    assert np.array_equal(ti, ti_ref[0]) and np.array_equal(coef, coef_ref[0])
+    blocks = table.slots[torch.from_numpy(ti + E).long().to(DEV)].cpu().numpy()
+    y = oracle.moe_decode(blocks, np.arange(10, dtype=np.int32), table.s2[1][torch.from_numpy(ti).long()].cpu().numpy(),
+                          coef, x.float().cpu().numpy()[0])
+    ref = oracle.shared_expert(*(t.float().cpu().numpy() for t in (x, wg, wu, wd, wsg)), y[None])
+    got = out.float().cpu().numpy()
+    assert rel_err(got, ref) <= 1e-2
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+    del g

@@ -126,3 +126,38 @@ def test_e4m3_rows_to_bf16_matches_reference_expression():
     nan_got = (got & 0x7FFF) > 0x7F80
     assert np.array_equal(nan_ref, nan_got)
     assert np.array_equal(got[~nan_ref], ref[~nan_ref])            # incl. signed zeros and bf16 subnormals
+
+
+def test_shared_expert_oracle_matches_reference_expression():
+    """oracle.shared_expert against the reference's own expression run by torch
+    on the CPU with bf16 tensors: sigmoid(F.linear(x, sh_g)) * sh_down(silu(
+    sh_gate(x)) * sh_up(x)) (qwen_engine.py:817-818, Lin = F.linear on bf16
+    weights, :84) and y.to(bf16) + sh (:829).  torch's CPU GEMMs sum in fp32,
+    the oracle exactly, so an element may sit one bf16 step apart; at most a
+    few in a thousand do."""
+    import torch.nn.functional as F
+    rng = np.random.Generator(np.random.PCG64(5))
+    T, I = 3, 256
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)
+    x, wg, wu = bf(rng.standard_normal((T, 2560))), bf(rng.standard_normal((I, 2560)) * .02), bf(rng.standard_normal((I, 2560)) * .02)
+    wd, wsg = bf(rng.standard_normal((2560, I)) * .02), bf(rng.standard_normal((1, 2560)) * .02)
+    y = torch.from_numpy(rng.standard_normal((T, 2560)).astype(np.float32))
+    sh = F.linear(F.silu(F.linear(x, wg)) * F.linear(x, wu), wd)
+    sh = torch.sigmoid(F.linear(x, wsg)) * sh
+    ref = (y.to(torch.bfloat16) + sh).float().numpy()
+    got = oracle.shared_expert(*(t.float().numpy() for t in (x, wg, wu, wd, wsg)), y.numpy())
+    ulp = np.abs(got.view(np.int32) - ref.view(np.int32))
+    assert ulp.max() <= 2 and (ulp > 0).mean() < 0.01, (ulp.max(), (ulp > 0).mean())
+
+
+def test_router_logits_oracle_matches_reference_expression():
+    """oracle.router_logits against F.linear(x, W_router) in bf16 on the CPU
+    (qwen_engine.py:803): equal to within one bf16 step, rarely apart."""
+    import torch.nn.functional as F
+    rng = np.random.Generator(np.random.PCG64(6))
+    x = torch.from_numpy(rng.standard_normal((4, 2560)).astype(np.float32)).to(torch.bfloat16)
+    w = torch.from_numpy((rng.standard_normal((512, 2560)) * .02).astype(np.float32)).to(torch.bfloat16)
+    ref = F.linear(x, w).float().numpy()
+    got = oracle.router_logits(x.float().numpy(), w.float().numpy())
+    ulp = np.abs(got.view(np.int32) - ref.view(np.int32))
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.02
