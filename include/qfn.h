@@ -209,6 +209,25 @@ int qfn_shared_expert(const uint16_t* x, int64_t T, const uint16_t* w_gate, cons
                       uint16_t* h, uint16_t* gt, uint16_t* out, qfn_stream_t stream);
 
 /*
+ * qfn_deltanet_step -- replaces recurrent_gated_delta_rule at T == 1
+ * (qwen_engine.py:158-174), the per-token state update of the DeltaNet
+ * layers (QwenEngine.deltanet, qwen_engine.py:718-719):
+ *   q = l2norm(q) / sqrt(dk), k = l2norm(k)     (l2norm: x * rsqrt(sum x^2 + 1e-6))
+ *   S[h] = S[h] * exp(g[h]); delta = (v[h] - S[h]^T k) * beta[h]
+ *   S[h] = S[h] + k delta^T;  out[h] = bf16(S[h]^T q)
+ *   q, k: bf16[n_key_heads][dk]; value head h uses key head
+ *         h / (n_heads / n_key_heads) (the engine's repeat_interleave);
+ *   v: bf16[n_heads][dv]; g: f32[n_heads]; beta: bf16[n_heads];
+ *   S: f32[n_heads][dk][dv], updated in place; out: bf16[n_heads][dv].
+ *   dk in {64, 128, 256}; dv % 32 == 0, dv <= 4096.  One launch (a
+ *   programmatic dependent: the state is read before the dependency wait,
+ *   so no earlier kernel of the stream may still write S).
+ */
+int qfn_deltanet_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                      const uint16_t* beta, float* S, uint16_t* out, int n_heads, int n_key_heads,
+                      int dk, int dv, qfn_stream_t stream);
+
+/*
  * qfn_gemv_e4m3 -- replaces fp8gemv.gemv (fp8gemv.py:20-26).
  *   y[n] = s[n] * sum_k e4m3(q[n][k]) * x[k], fp32 accumulation.
  *   q: u8[N][K] (float8_e4m3fn bytes) device, 16-byte aligned, K % 16 == 0.

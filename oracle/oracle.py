@@ -213,3 +213,24 @@ def shared_expert(x, wg, wu, wd, wsg, y=None):
     if y is None:
         return sh
     return bf16_round(bf16_round(_c(y, np.float32)) + sh)
+
+
+def deltanet_step(q, k, v, g, beta, S):
+    """recurrent_gated_delta_rule at T == 1 (qwen_engine.py:158-174) in fp64,
+    the state updated in place and the output rounded to bf16.
+    q, k [Hk, dk]; v [H, dv]; g, beta [H]; S [H, dk, dv] float64 (in/out);
+    value head h uses key head h // (H // Hk) (repeat_interleave, :717).
+    Returns out [H, dv] (bf16 values as fp32)."""
+    q, k = np.asarray(q, np.float64), np.asarray(k, np.float64)
+    H, dk = S.shape[0], S.shape[1]
+    r = H // q.shape[0]
+    q = q / np.sqrt((q * q).sum(-1, keepdims=True) + 1e-6) / np.sqrt(dk)
+    k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+    out = np.empty((H, S.shape[2]), np.float64)
+    for h in range(H):
+        qh, kh = q[h // r], k[h // r]
+        S[h] *= np.exp(np.float64(g[h]))
+        delta = (np.asarray(v[h], np.float64) - kh @ S[h]) * np.float64(beta[h])
+        S[h] += np.outer(kh, delta)
+        out[h] = qh @ S[h]
+    return bf16_round(out.astype(np.float32))

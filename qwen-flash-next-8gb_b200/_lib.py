@@ -35,6 +35,7 @@ SIGNATURES = {
     "qfn_prefill_status": [_P, _I],
     "qfn_moe_route": [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "qfn_shared_expert": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
+    "qfn_deltanet_step": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
 }
 # entry points whose return value is not an int status
 RESTYPES = {"qfn_moe_prefill_workspace": ctypes.c_size_t}

@@ -142,3 +142,25 @@ def expert_block(layer, expert, seed, dev):
     """The synthetic block of (layer, expert) as a new CUDA u8[BLOCK] tensor
     (what fill_table_gpu wrote into whichever table holds it)."""
     return fill_block_gpu(torch.empty(BLOCK, dtype=torch.uint8, device=dev), block_seed(seed, layer, expert))
+
+
+def deltanet_inputs(steps, heads, key_heads, dk, dv, seed):
+    """Seeded inputs of `steps` one-token delta-rule steps (qwen_engine.py:696-719
+    at T == 1): q, k bf16 [steps, key_heads, dk] and v bf16 [steps, heads, dv]
+    ~ silu(N(0, 1)) (the conv output's activation); g fp32 [steps, heads] =
+    -exp(A_log) * softplus(a + dt_bias) with A_log ~ U(-2, 1), a + dt_bias ~
+    N(0, 1); beta bf16 [steps, heads] = sigmoid(N(0, 1)); S0 fp32 [heads, dk, dv]
+    ~ N(0, 0.05).  CPU torch tensors."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+
+    def silu_bf16(shape):
+        z = rng.standard_normal(shape).astype(np.float32)
+        return torch.from_numpy(z / (1 + np.exp(-z))).to(torch.bfloat16)
+
+    q, k, v = silu_bf16((steps, key_heads, dk)), silu_bf16((steps, key_heads, dk)), silu_bf16((steps, heads, dv))
+    a_log = rng.uniform(-2, 1, size=heads).astype(np.float32)
+    a = rng.standard_normal((steps, heads)).astype(np.float32)
+    g = torch.from_numpy((-np.exp(a_log) * np.log1p(np.exp(a))).astype(np.float32))
+    beta = torch.from_numpy(1 / (1 + np.exp(-rng.standard_normal((steps, heads))))).float().to(torch.bfloat16)
+    S0 = torch.from_numpy((rng.standard_normal((heads, dk, dv)) * 0.05).astype(np.float32))
+    return q, k, v, g, beta, S0

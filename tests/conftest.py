@@ -54,3 +54,11 @@ def sha(a):
         a = a.copy()
         a[np.isnan(a)] = np.float32("nan")
     return hashlib.sha256(a.tobytes()).hexdigest()
+
+
+def bf16_steps(a, b):
+    """Distance in bf16 rounding steps between arrays of bf16 values held as
+    fp32 (|difference of the top 16 bits of the patterns|; same-sign values)."""
+    a = np.ascontiguousarray(a, np.float32).view(np.int32) >> 16
+    b = np.ascontiguousarray(b, np.float32).view(np.int32) >> 16
+    return np.abs(a.astype(np.int64) - b.astype(np.int64))

@@ -28,7 +28,7 @@ if not REF or not os.path.exists(os.path.join(REF, "qmoe.py")):
     sys.exit("set QFN_REFERENCE to the reference project root")
 sys.path.insert(0, REF)
 import qmoe  # noqa: E402  (the reference's module)
-from qwen_engine import to_fp8_rows  # noqa: E402
+from qwen_engine import recurrent_gated_delta_rule, to_fp8_rows  # noqa: E402
 
 spec = importlib.util.spec_from_file_location("synthetic", os.path.join(REPO, "qwen-flash-next-8gb_b200",
                                                                       "synthetic.py"))
@@ -61,6 +61,21 @@ def ref_route(logits, topk=10):
     tv, ti = torch.topk(probs, topk, dim=-1)
     tv = (tv / tv.sum(-1, keepdim=True)).to(torch.bfloat16)
     return ti, tv
+
+
+def deltanet_golden(C):
+    steps, H, Hk, dk, dv, seed = 8, 4, 2, 128, 128, 71
+    q, k, v, g, beta, S = synthetic.deltanet_inputs(steps, H, Hk, dk, dv, seed)
+    S = S[None].clone()
+    outs = []
+    for t in range(steps):
+        qr = q[t].repeat_interleave(H // Hk, dim=0)[None, None]
+        kr = k[t].repeat_interleave(H // Hk, dim=0)[None, None]
+        o, S = recurrent_gated_delta_rule(qr, kr, v[t][None, None], g[t][None, None], beta[t][None, None], S)
+        outs.append(o[0, 0].float().numpy())
+    save("deltanet_out", np.stack(outs))
+    save("deltanet_state", S[0].numpy())
+    C["deltanet"] = {"steps": steps, "heads": H, "key_heads": Hk, "dk": dk, "dv": dv, "seed": seed}
 
 
 def main():
@@ -172,10 +187,23 @@ def main():
     C["prefill_t8"] = {"T": T, "experts": E, "topk": k, "table_seed": 51, "s2_seed": 52, "x_seed": 53,
                        "logit_seed": 54}
 
+    # 9. the one-token gated delta rule (qwen_engine.py:158-174) over 8 steps, the
+    #    state carried from step to step; q, k repeated over the value heads as the
+    #    engine does (qwen_engine.py:717)
+    deltanet_golden(C)
+
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote", len(C), "cases")
 
 
-if __name__ == "__main__":
+if __name__ == "__main__" and sys.argv[1:] == ["deltanet"]:
+    # add only the delta-rule case to an existing golden.json
+    with open(os.path.join(HERE, "golden.json")) as f:
+        meta = json.load(f)
+    deltanet_golden(meta["cases"])
+    with open(os.path.join(HERE, "golden.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("added deltanet")
+elif __name__ == "__main__":
     main()

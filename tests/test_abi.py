@@ -98,6 +98,12 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert sh(fake, 320) == 4
     assert sh(fake, 8192) == 4
     assert sh(odd, 512) == 2
+    # delta rule: nulls, head ratio, dk / dv
+    dn = lambda H, Hk, dk, dv: lib.qfn_deltanet_step(fake, fake, fake, fake, fake, fake, fake, H, Hk, dk, dv, None)
+    assert lib.qfn_deltanet_step(None, fake, fake, fake, fake, fake, fake, 4, 2, 128, 128, None) == 1
+    assert dn(4, 3, 128, 128) == 1
+    assert dn(4, 2, 96, 128) == 4
+    assert dn(4, 2, 128, 100) == 4
 
 
 def test_python_wrappers_reject_cpu_tensors():

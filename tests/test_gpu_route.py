@@ -19,7 +19,7 @@ import oracle
 import qmoe
 import routing
 import synthetic
-from conftest import rel_err
+from conftest import bf16_steps, rel_err
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -48,7 +48,7 @@ def test_route_fused_matches_oracle(T, E, topk, seed):
     torch.cuda.synchronize()
     logits = r["logits"].float().cpu().numpy()
     exact = oracle.router_logits(x.float().cpu().numpy(), w.float().cpu().numpy())
-    steps = np.abs(logits.view(np.int32) - exact.view(np.int32))
+    steps = bf16_steps(logits, exact)
     assert steps.max() <= 1 and (steps > 0).mean() < 0.02
     ti_ref, coef_ref = oracle.route(logits, topk)
     ti = r["ti"].cpu().numpy()
@@ -92,7 +92,7 @@ def test_shared_expert_matches_oracle(T, I, seed, with_y):
     ref = oracle.shared_expert(*(t.float().cpu().numpy() for t in (x, wg, wu, wd, wsg)),
                                y.cpu().numpy() if with_y else None)
     got = out.float().cpu().numpy()
-    steps = np.abs(got.view(np.int32) - ref.view(np.int32))
+    steps = bf16_steps(got, ref)
     assert np.isfinite(got).all()
     assert rel_err(got, ref) <= 1e-2      # a few bf16 steps at most, relative to RMS
     assert (steps > 0).mean() < 0.02

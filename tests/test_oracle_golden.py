@@ -6,7 +6,7 @@ import torch
 
 import oracle
 import synthetic
-from conftest import rel_err, sha
+from conftest import bf16_steps, rel_err, sha
 
 
 def test_e4m3_decode_table_bit_exact(golden):
@@ -146,7 +146,7 @@ def test_shared_expert_oracle_matches_reference_expression():
     sh = torch.sigmoid(F.linear(x, wsg)) * sh
     ref = (y.to(torch.bfloat16) + sh).float().numpy()
     got = oracle.shared_expert(*(t.float().numpy() for t in (x, wg, wu, wd, wsg)), y.numpy())
-    ulp = np.abs(got.view(np.int32) - ref.view(np.int32))
+    ulp = bf16_steps(got, ref)
     assert ulp.max() <= 2 and (ulp > 0).mean() < 0.01, (ulp.max(), (ulp > 0).mean())
 
 
@@ -159,5 +159,22 @@ def test_router_logits_oracle_matches_reference_expression():
     w = torch.from_numpy((rng.standard_normal((512, 2560)) * .02).astype(np.float32)).to(torch.bfloat16)
     ref = F.linear(x, w).float().numpy()
     got = oracle.router_logits(x.float().numpy(), w.float().numpy())
-    ulp = np.abs(got.view(np.int32) - ref.view(np.int32))
+    ulp = bf16_steps(got, ref)
     assert ulp.max() <= 1 and (ulp > 0).mean() < 0.02
+
+
+def test_deltanet_oracle_matches_reference(golden):
+    """oracle.deltanet_step (fp64) against the reference's recurrent_gated_delta_rule
+    (torch fp32 on the CPU, qwen_engine.py:158-174) over 8 carried steps: the
+    bf16 outputs agree to one bf16 step, the fp32 state to fp32 rounding."""
+    c = golden.cases["deltanet"]
+    q, k, v, g, beta, S0 = synthetic.deltanet_inputs(c["steps"], c["heads"], c["key_heads"], c["dk"], c["dv"], c["seed"])
+    S = S0.double().numpy().copy()
+    ref_out = golden.load("deltanet_out")
+    for t in range(c["steps"]):
+        o = oracle.deltanet_step(q[t].float().numpy(), k[t].float().numpy(), v[t].float().numpy(), g[t].numpy(),
+                                 beta[t].float().numpy(), S)
+        steps = bf16_steps(o, ref_out[t])
+        assert steps.max() <= 1 and (steps > 0).mean() < 0.02
+    ref_S = golden.load("deltanet_state")
+    assert np.abs(S - ref_S).max() / np.sqrt(np.mean(ref_S.astype(np.float64) ** 2)) < 1e-5
