@@ -40,7 +40,7 @@
 namespace qfn {
 
 constexpr int kPfRows = 128;           // pairs per tile (MMA N <= 128) and A rows (MMA M)
-constexpr int kPfThreads = 512;  // 16 warps: 2 producers, 2 MMA issuers, 8 dequantisers, 4 epilogue
+constexpr int kPfThreads = 512;  // 16 warps: 2 producers, 1 MMA issuer, 8 dequantisers, 4 epilogue (1 spare)
 constexpr int kPfMaxExperts = 1024;
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   using C = PfCfg<MODE>;
   using L = PfSmem<MODE>;
   constexpr int KS = C::kKStages, SK = C::kStageKB, RS = C::kRStages, KB = C::kKBlocks, NST = KB / SK;
-  constexpr int NI = MODE == kGateUp ? 2 : 1;  // MMA issuers (gate/up: one for the gate rows, one for the up rows)
+  constexpr int NI = 1;  // MMA issuers: one warp (a second issuing warp halves each one's MMA rate)
   static_assert(KB % SK == 0 && C::kRawKB % SK == 0 || SK % C::kRawKB == 0, "stage / raw stage sizes");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -507,12 +507,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         __syncwarp();
       }
     }
-  } else if (warp == 1 || (MODE == kGateUp && warp == 2)) {
-    // ---------------- MMA issuers (one elected lane of the warp issues).
-    // Gate/up: warp 1 the gate accumulator, warp 2 the up accumulator (two
-    // issuers nearly double the MMA issue rate); down: warp 1.  Each issuer
-    // commits once per stage (k_empty counts NI commits) and once per job.
-    const int g = warp - 1;  // 0: gate (or down), 1: up
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one elected lane of warp 1 issues).  Gate/up:
+    // the gate and the up accumulators, interleaved per k-step.  A single
+    // issuing warp: measured on this part (M = 128, K = 16, A in TMEM), one
+    // warp issues an MMA every 24 (N = 16) to 32 (N = 64) cycles, while two
+    // warps issuing into separate accumulators take ~56 cycles per MMA.  Commits
+    // once per stage (k_empty) and once per job (tm_full).
+    constexpr int NG = MODE == kGateUp ? 2 : 1;
     int st = 0;
     PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
@@ -528,7 +530,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (h != 1) pf_wait(&tm_empty[0], (hv.u0 & 1) ^ 1, abort);
       if (h != 0) pf_wait(&tm_empty[1], (hv.u1 & 1) ^ 1, abort);
       tc_fence_after();
-      const uint32_t d = tmem + (h == 1 ? 128u : 0u) + (g ? (h == 2 ? 128u : 64u) : 0u);
+      const uint32_t d0 = tmem + (h == 1 ? 128u : 0u);
+      const uint32_t d1 = d0 + (h == 2 ? 128u : 64u);   // gate/up: the up accumulator
       // B descriptors differ only in the start address field (address / 16):
       // +2 per k-step of 16, +jstep per K-block, +lostep for the h lo rows.
       const uint64_t bdesc0 = umma_desc_sw128(smem_u32(smem + L::kB), 1024);
@@ -538,16 +541,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         pf_wait(&k_full[s], (st / KS) & 1, abort);
         tc_fence_after();
         if (elect_one()) {
-          const uint32_t a = tmem + kPfTmemA + C::kASlot * s + 32 * g;
+          const uint32_t a = tmem + kPfTmemA + C::kASlot * s;
           const uint64_t bd = bdesc0 + static_cast<uint32_t>((s * C::kBMax) >> 4);
 #pragma unroll
           for (int j = 0; j < SK; ++j) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const uint32_t ak = a + (MODE == kGateUp ? 64u : 32u) * j + 8 * k;
               const uint64_t bk = bd + (j * jstep + 2 * k);
-              mma_f16_ta(d, ak, bk, idesc, (j | k) != 0 || q > 0);
-              if (split) mma_f16_ta(d, ak, bk + lostep, idesc, true);
+              const bool acc = (j | k) != 0 || q > 0;
+#pragma unroll
+              for (int g = 0; g < NG; ++g) {
+                const uint32_t ak = a + (MODE == kGateUp ? 64u : 32u) * j + 32 * g + 8 * k;
+                mma_f16_ta(g ? d1 : d0, ak, bk, idesc, acc);
+                if (split) mma_f16_ta(d0, ak, bk + lostep, idesc, true);
+              }
             }
           }
           mma_commit(&k_empty[s]);
