@@ -104,7 +104,9 @@ __global__ void __launch_bounds__(32 * kRtWarps) moe_route_select_kernel(
   float sum = 0.f;
 #pragma unroll
   for (int j = 0; j < kRtMaxExperts / 32; ++j) {
-    p[j] = (j < per && lane + 32 * j < E) ? expf(p[j] - mx) : 0.f;
+    // exp in double, rounded once to fp32 (correctly rounded in practice): the
+    // closest one value per logit that torch's fp32 exp and the host's can land on
+    p[j] = (j < per && lane + 32 * j < E) ? static_cast<float>(exp(static_cast<double>(p[j] - mx))) : 0.f;
     sum += p[j];
   }
   sum = warp_sum(sum);

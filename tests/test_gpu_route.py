@@ -5,10 +5,12 @@ and the whole device-side block (moe_block.DecodeMoE) against the CPU oracle.
 
 Router: the logits are the bf16 rounding of fp32 dot products, so they may sit
 one bf16 step from the exact value (oracle.router_logits) when a sum lies next
-to a rounding boundary; the top-k and the bf16 weights computed from the
-kernel's logits must equal the oracle's router (oracle.route, the reference's
-softmax / topk / renormalisation) exactly, and the torch expression of the
-reference on the same logits.
+to a rounding boundary.  From the kernel's logits, the chosen experts must
+equal the oracle's router (oracle.route, the reference's softmax / topk /
+renormalisation) exactly, and the bf16 weights must equal them to within one
+bf16 step: the softmax's exp and sums are fp32 with their own rounding order
+(the reference's torch CPU and CUDA softmaxes differ from each other the
+same way), so a weight next to a bf16 rounding boundary may round either way.
 """
 import numpy as np
 import pytest
@@ -27,6 +29,11 @@ DEV = "cuda"
 
 def bf16(a):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).to(DEV)
+
+
+def assert_weights_close(a, b):
+    st = bf16_steps(a, b)
+    assert st.max() <= 1 and (st > 0).mean() <= 0.05, (st.max(), (st > 0).mean())
 
 
 def router_case(T, E, seed, dup_rows=0):
@@ -53,16 +60,16 @@ def test_route_fused_matches_oracle(T, E, topk, seed):
     ti_ref, coef_ref = oracle.route(logits, topk)
     ti = r["ti"].cpu().numpy()
     assert np.array_equal(ti, ti_ref)
-    assert np.array_equal(r["tv"].float().cpu().numpy(), coef_ref)
+    assert_weights_close(r["tv"].float().cpu().numpy(), coef_ref)
     # the reference's torch expression on the same logits: the same experts and weights
     # (torch.topk on CUDA may list experts of equal probability in either order)
     ti_t, tv_t = routing.route(r["logits"], topk)
     o_t, o = np.argsort(ti_t.cpu().numpy(), 1), np.argsort(ti, 1)
     assert np.array_equal(np.take_along_axis(ti_t.cpu().numpy(), o_t, 1), np.take_along_axis(ti, o, 1))
-    assert np.array_equal(np.take_along_axis(tv_t.float().cpu().numpy(), o_t, 1),
-                          np.take_along_axis(r["tv"].float().cpu().numpy(), o, 1))
+    assert_weights_close(np.take_along_axis(tv_t.float().cpu().numpy(), o_t, 1),
+                         np.take_along_axis(r["tv"].float().cpu().numpy(), o, 1))
     assert np.array_equal(r["sidx"].cpu().numpy(), ti + layer * E)
-    assert np.array_equal(r["coef"].cpu().numpy(), coef_ref)
+    assert np.array_equal(r["coef"].cpu().numpy(), r["tv"].float().cpu().numpy())
     assert torch.equal(r["s2"], s2_table[layer][r["ti"].long()])
 
 
@@ -72,7 +79,7 @@ def test_route_fused_ties_go_to_the_lower_expert():
     logits = r["logits"].float().cpu().numpy()
     ti_ref, coef_ref = oracle.route(logits, 10)
     assert np.array_equal(r["ti"].cpu().numpy(), ti_ref)
-    assert np.array_equal(r["tv"].float().cpu().numpy(), coef_ref)
+    assert_weights_close(r["tv"].float().cpu().numpy(), coef_ref)
     assert (r["ti"].cpu().numpy() < 256).all()
 
 
@@ -130,7 +137,8 @@ def test_decode_moe_block_device_only_in_a_graph():
     coef = blk.route_buf["tv"][0].float().cpu().numpy()
     logits = blk.route_buf["logits"].float().cpu().numpy()
     ti_ref, coef_ref = oracle.route(logits, 10)
-    assert np.array_equal(ti, ti_ref[0]) and np.array_equal(coef, coef_ref[0])
+    assert np.array_equal(ti, ti_ref[0])
+    assert_weights_close(coef, coef_ref[0])
     blocks = table.slots[torch.from_numpy(ti + E).long().to(DEV)].cpu().numpy()
     y = oracle.moe_decode(blocks, np.arange(10, dtype=np.int32), table.s2[1][torch.from_numpy(ti).long()].cpu().numpy(),
                           coef, x.float().cpu().numpy()[0])
