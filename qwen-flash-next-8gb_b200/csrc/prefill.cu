@@ -40,7 +40,18 @@
 namespace qfn {
 
 constexpr int kPfRows = 128;           // pairs per tile (MMA N <= 128) and A rows (MMA M)
-constexpr int kPfThreads = 512;  // 16 warps: 2 producers, 1 MMA issuer, 8 dequantisers, 4 epilogue (1 spare)
+#ifndef PF_DEQ_WARPS
+#define PF_DEQ_WARPS 16
+#endif
+// Warps: 0 activation producer, 1 MMA issuer, 2 spare, 3 weight producer,
+// 4 .. 4 + kPfDeq - 1 dequantisers, the last 4 the epilogue.  The dequantisers
+// come in groups of 8 (4 lane quarters x 2 matrices or K halves); with 16 the
+// two groups take alternate K-blocks of a stage (twice the warps to hide the
+// latency of the conversion chains: it is latency-, not issue-bound).
+constexpr int kPfDeq = PF_DEQ_WARPS;
+constexpr int kPfDeqSplit = kPfDeq / 8;
+constexpr int kPfEpi0 = 4 + kPfDeq;                 // first epilogue warp
+constexpr int kPfThreads = 32 * (kPfEpi0 + 4);
 constexpr int kPfMaxExperts = 1024;
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
@@ -394,17 +405,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   constexpr int KS = C::kKStages, SK = C::kStageKB, RS = C::kRStages, KB = C::kKBlocks, NST = KB / SK;
   constexpr int NI = 1;  // MMA issuers: one warp (a second issuing warp halves each one's MMA rate)
   static_assert(KB % SK == 0 && C::kRawKB % SK == 0 || SK % C::kRawKB == 0, "stage / raw stage sizes");
+  static_assert(SK % kPfDeqSplit == 0 && C::kRawKB % kPfDeqSplit == 0, "dequantiser groups share a stage's K-blocks");
+  static_assert(SK <= C::kRawKB, "a stage ends at most one raw stage");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   // stage s: activation tile s in shared memory + A slot s in TMEM.
-  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + 8 dequant warps
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::kBar);  // producer (tx) + the dequant warps
   uint64_t* k_empty = k_full + KS;   // NI MMA issuers (commit)
   uint64_t* r_full = k_empty + KS;
-  uint64_t* r_empty = r_full + RS;   // 8 dequant warps
+  uint64_t* r_empty = r_full + RS;   // the dequant warps
   uint64_t* tm_full = r_empty + RS;  // [2] accumulator halves: NI MMA issuers -> epilogue
   uint64_t* tm_empty = tm_full + 2;  // [2] 4 epilogue warps
   uint64_t* js_full = tm_empty + 2;  // [2] down: per-job scale rows
-  uint64_t* js_empty = js_full + 2;  // [2] 8 dequant warps
+  uint64_t* js_empty = js_full + 2;  // [2] the dequant warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(js_empty + 2);
   volatile uint32_t* abort = tslot + 1;
   int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][2][128]: per-column factors (epilogue)
@@ -413,18 +426,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     *abort = 0u;
     for (int s = 0; s < KS; ++s) {
-      mbar_init(&k_full[s], 9);
+      mbar_init(&k_full[s], 2);   // the activation producer (tx) + one arrival for all dequantisers
       mbar_init(&k_empty[s], NI);
     }
     for (int s = 0; s < RS; ++s) {
       mbar_init(&r_full[s], 1);
-      mbar_init(&r_empty[s], 8);
+      mbar_init(&r_empty[s], 1);  // one arrival for all dequantisers
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&tm_full[h], NI);
       mbar_init(&tm_empty[h], 4);
       mbar_init(&js_full[h], 1);
-      mbar_init(&js_empty[h], 8);
+      mbar_init(&js_empty[h], 1);
     }
     fence_mbar_init();
   }
@@ -568,15 +581,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       hv.done(h);
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < kPfEpi0) {
     // ---------------- dequantisers: warp 4 + w writes TMEM lanes 32 (w % 4) ..
-    // + 31 of the A slot, both K-blocks of the stage.  Gate/up: matrix
-    // i = w / 4 (gate / up rows of the job's 128 features), 64 k per K-block;
-    // down: K half i = w / 4 (32 k) of the job's 128 output rows.  A warp
-    // converts the stage into registers before it waits for the A slot, so
-    // the conversion overlaps the MMAs of the previous stage.
+    // + 31 of the A slot, K-blocks kbs, kbs + kPfDeqSplit, ... of each stage
+    // (group kbs = w / 8).  Gate/up: matrix i = (w / 4) % 2 (gate / up rows of
+    // the job's 128 features), 64 k per K-block; down: K half i (32 k) of the
+    // job's 128 output rows.  A warp converts its K-blocks of the stage into
+    // registers before it waits for the A slot, so the conversion overlaps the
+    // MMAs of the previous stage.
+    constexpr int SKT = SK / kPfDeqSplit;  // K-blocks of a stage per thread
     const int w = warp - 4;
-    const int i = w >> 2;
+    const int kbs = w >> 3;
+    const int i = (w >> 2) & 1;
     const int r = 32 * (w & 3) + lane;    // A row = TMEM lane
     const int d = 128 * i + r;            // gate/up: row of the raw stage ([gate|up][128])
     // raw row of this thread in a raw stage (gate/up: 128-byte rows, 128-byte
@@ -592,15 +608,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
       for (int q = 0; q < NST; ++q, ++st) {
         const int s = st % KS;
-        uint32_t v[SK][NV];
+        uint32_t v[SKT][NV];
 #pragma unroll
-        for (int j = 0; j < SK; ++j) {
-          const int kb = SK * q + j;
+        for (int jt = 0; jt < SKT; ++jt) {
+          const int kb = SK * q + kbs + kPfDeqSplit * jt;
           const int gkb = jj * KB + kb;  // K-blocks of this CTA so far
           const int rt = gkb / C::kRawKB, sr = rt % RS;
           const int kr = kb % C::kRawKB;  // K-block within the raw stage
           const uint8_t* stage = smem + L::kRaw + sr * C::kRaw;
-          if (kr == 0) {
+          if (kr < kPfDeqSplit) {   // this thread's first K-block of the raw stage
             pf_wait(&r_full[sr], (rt / RS) & 1, abort);
             if (MODE == kGateUp) sc = *reinterpret_cast<const uint4*>(stage + C::kRawBytes + 16 * d);
           }
@@ -620,7 +636,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               e2m1x8_to_f16x2(words[jq], hf);
               const uint32_t sc2 = jq < 2 ? sa0 : (jq < 4 ? sa1 : (jq < 6 ? sa2 : sa3));
 #pragma unroll
-              for (int e = 0; e < 4; ++e) v[j][(4 * jq + e) % NV] = hmul2_u32(hf[e], sc2);
+              for (int e = 0; e < 4; ++e) v[jt][(4 * jq + e) % NV] = hmul2_u32(hf[e], sc2);
             }
           } else {
             const uint4 w0 = *reinterpret_cast<const uint4*>(raw + (((2 * kr + i) ^ swz) << 4));
@@ -632,35 +648,39 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               e2m1x8_to_f16x2(words[jq], hf);
               const uint32_t sc2 = jq < 2 ? s0 : s1;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) v[j][4 * jq + e] = hmul2_u32(hf[e], sc2);
+              for (int e = 0; e < 4; ++e) v[jt][4 * jq + e] = hmul2_u32(hf[e], sc2);
             }
-          }
-          if (kr == C::kRawKB - 1) {  // last K-block of the raw stage: release it
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&r_empty[sr]);
           }
         }
         pf_wait(&k_empty[s], ((st / KS) & 1) ^ 1, abort);
         tc_fence_after();
         const uint32_t aslot = tmem + kPfTmemA + C::kASlot * s + lane_base;
 #pragma unroll
-        for (int j = 0; j < SK; ++j) {
-          if (MODE == kGateUp) tmem_st_x32(aslot + 64 * j + 32 * i, *reinterpret_cast<uint32_t(*)[32]>(v[j]));
-          else tmem_st_x16(aslot + 32 * j + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(v[j]));
+        for (int jt = 0; jt < SKT; ++jt) {
+          const int j = kbs + kPfDeqSplit * jt;
+          if (MODE == kGateUp) tmem_st_x32(aslot + 64 * j + 32 * i, *reinterpret_cast<uint32_t(*)[32]>(v[jt]));
+          else tmem_st_x16(aslot + 32 * j + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(v[jt]));
         }
         tmem_st_wait();
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
+        // All dequantiser warps meet on a named barrier and one thread signals
+        // the MMA issuer (and releases the raw stage and the job's scale rows
+        // when this stage used their last K-block): one mbarrier arrival per
+        // handoff instead of one per warp (arrivals on one mbarrier serialise).
+        asm volatile("bar.sync 2, %0;" ::"n"(32 * kPfDeq) : "memory");
+        if (w == 0 && lane == 0) {
           mbar_arrive(&k_full[s]);
+          const int last_kb = SK * q + SK - 1;
+          if (last_kb % C::kRawKB == C::kRawKB - 1)
+            mbar_arrive(&r_empty[((jj * KB + last_kb) / C::kRawKB) % RS]);
           if (MODE == kDown && q == NST - 1) mbar_arrive(&js_empty[jj & 1]);
         }
       }
     }
-  } else if (warp >= 12) {
-    // ---------------- epilogue: warp 12 + q reads TMEM lanes 32q .. 32q + 31
-    const int q = warp - 12;
-    const int et = threadIdx.x - 384;  // 0..127
+  } else if (warp >= kPfEpi0) {
+    // ---------------- epilogue: warp kPfEpi0 + q reads TMEM lanes 32q .. 32q + 31
+    const int q = warp - kPfEpi0;
+    const int et = threadIdx.x - 32 * kPfEpi0;  // 0..127
     int jj = 0;
     PfHalves<MODE> hv;
     for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
