@@ -93,6 +93,11 @@ def parse():
     p.add_argument("--ep-mode", default="ag", choices=["ag", "a2a"],
                    help="expert-parallel exchange: ag = all-gather + reduce-scatter (no host sync), "
                         "a2a = all-to-all of routed rows (host sync for split sizes)")
+    p.add_argument("--ep-chunks", type=int, default=2,
+                   help="ag exchange: token slices pipelined so one slice's exchange overlaps another's GEMMs")
+    p.add_argument("--ep-sm-budget", type=int, default=-16,
+                   help="SMs for the persistent prefill GEMMs under expert parallelism with --ep-chunks > 1 "
+                        "(<= 0: all SMs minus that many, left to NCCL's kernels)")
     p.add_argument("--placement", default="lpt", choices=["lpt", "contiguous"],
                    help="expert placement over ranks for prefill: load-aware (LPT) or contiguous ranges")
     p.add_argument("--parity-tokens", type=int, default=16, help="tokens per rank checked against the oracle")
@@ -364,7 +369,15 @@ def prefill_record(ctx):
         table = ExpertTable(K=TOPK, dev=dev, n_layers=1, n_experts=shard.per_rank)
         table.fill_synthetic(seed=args.seed, experts=shard.experts)
         s2 = table.s2[0]
-        ep_fn = ep.moe_prefill_ep_ag if args.ep_mode == "ag" else ep.moe_prefill_ep
+        if args.ep_mode == "ag":
+            ep_fn = lambda *a: ep.moe_prefill_ep_ag(*a, chunks=args.ep_chunks)
+            ep_fn.__name__ = "moe_prefill_ep_ag"
+            if args.ep_chunks > 1:
+                import _lib
+                sms = torch.cuda.get_device_properties(dev).multi_processor_count
+                _lib.set_prefill_sm_budget(args.ep_sm_budget if args.ep_sm_budget > 0 else sms + args.ep_sm_budget)
+        else:
+            ep_fn = ep.moe_prefill_ep
     xs, tis, tvs = zipf_routes(dev, args.seed + 7, args.seed + 8 + 1000 * rank, T, R)
 
     def call(x, ti, tv):
@@ -418,6 +431,8 @@ def prefill_record(ctx):
     E = min(args.e2e_steps, args.steps)
     ms_e2e = ctx.timed(e2e_step, E, 2)
 
+    breakdown = ep_breakdown(ctx, shard, table, s2, xs[0], tis[0], tvs[0]) if shard is not None and \
+        args.ep_mode == "ag" else None
     rec = {
         "metric": PF_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -448,11 +463,48 @@ def prefill_record(ctx):
     if shard is not None:
         mean_pairs = T * TOPK
         rec["config"]["pairs_per_rank_max_over_mean"] = ctx.max_over_ranks(sum(pairs_rank) / R) / mean_pairs
+        rec["config"]["ep_chunks"] = args.ep_chunks if args.ep_mode == "ag" else None
+        rec["config"]["ep_breakdown_ms"] = breakdown
     if world == 1 and not args.no_cpu_baseline:
         rec["cpu_baseline"] = prefill_cpu_baseline(ctx, xs[0], tis[0], tvs[0])
     if not parity["pass"]:
         ctx.failed.append("prefill")
     return rec
+
+
+def ep_breakdown(ctx, shard, table, s2, x, ti, tv, reps=10):
+    """The unpipelined all-gather exchange's parts timed one at a time (max over ranks,
+    CUDA events): the two all-gathers, the grouped GEMM on the gathered tokens, the
+    reduce-scatter of the fp32 sums -- what the expert-parallel step is made of."""
+    import torch
+    import qmoe
+    import _lib
+    dist, dev, N = ctx.dist, ctx.dev, ctx.world
+    T, K = ti.shape
+    x_all = torch.empty(N * T, x.shape[1], dtype=x.dtype, device=dev)
+    meta = torch.cat([ti.to(torch.int32), tv.float().contiguous().view(torch.int32)], 1).contiguous()
+    meta_all = torch.empty(N * T, 2 * K, dtype=torch.int32, device=dev)
+    out = torch.empty(T, x.shape[1], dtype=torch.float32, device=dev)
+    mine = shard.maps(dev)[2]
+
+    def gather():
+        dist.all_gather_into_tensor(x_all, x.contiguous())
+        dist.all_gather_into_tensor(meta_all, meta)
+
+    gather()
+    ti_loc = mine[meta_all[:, :K].long()]
+    tv_all = meta_all[:, K:].contiguous().view(torch.float32)
+    _lib.set_prefill_sm_budget(0)
+    y = qmoe.moe_prefill(x_all, ti_loc, tv_all, table.slots, s2, 0)
+    parts = {"all_gather": gather,
+             "grouped_gemm": lambda: qmoe.moe_prefill(x_all, ti_loc, tv_all, table.slots, s2, 0),
+             "reduce_scatter": lambda: dist.reduce_scatter_tensor(out, y)}
+    res = {k: round(ctx.timed(lambda i, f=f: f(), reps, 2), 4) for k, f in parts.items()}
+    if ctx.args.ep_chunks > 1:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        b = ctx.args.ep_sm_budget
+        _lib.set_prefill_sm_budget(b if b > 0 else sms + b)
+    return res
 
 
 def ctx_all_gather(ctx, t):

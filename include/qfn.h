@@ -286,6 +286,15 @@ int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_is_int64,
                     qfn_stream_t stream);
 
 /*
+ * qfn_set_prefill_sm_budget -- for the current device, run the persistent
+ * grouped-GEMM kernels of qfn_moe_prefill on at most n_sms CTAs (0 = one per
+ * SM, the default), leaving the other SMs to kernels that should run at the
+ * same time: an expert-parallel caller overlapping NCCL collectives with the
+ * GEMMs of another chunk of tokens.  No counterpart in the reference.
+ */
+int qfn_set_prefill_sm_budget(int n_sms);
+
+/*
  * qfn_prefill_status -- read (and with clear != 0 reset) the prefill status
  * word of the current device: bit 0 = a bounded wait ran out (outputs of that
  * call invalid), bit 2 = an expert id outside [0, n_experts) was skipped.

@@ -33,6 +33,7 @@ SIGNATURES = {
     "qfn_moe_prefill_workspace": [_I64, _I, _I],
     "qfn_moe_prefill": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P],
     "qfn_prefill_status": [_P, _I],
+    "qfn_set_prefill_sm_budget": [_I],
     "qfn_moe_route": [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "qfn_shared_expert": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
     "qfn_deltanet_step": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
@@ -86,6 +87,11 @@ def prefill_status(clear=True):
     v = ctypes.c_uint(0)
     check(lib().qfn_prefill_status(ctypes.byref(v), int(clear)), "qfn_prefill_status")
     return v.value
+
+
+def set_prefill_sm_budget(n_sms):
+    """Persistent prefill GEMMs on at most n_sms SMs of the current device (0 = all)."""
+    check(lib().qfn_set_prefill_sm_budget(int(n_sms)), "qfn_set_prefill_sm_budget")
 
 
 def stream_of(t):

@@ -18,6 +18,7 @@ struct DeviceInfo {
   int sm_count;
   int cc_major, cc_minor;
   size_t smem_optin;
+  int pf_ctas;   // CTAs of the persistent prefill GEMMs (qfn_set_prefill_sm_budget; 0 = one per SM)
 };
 
 // Properties of the current device (cached per device).  Returns QFN_OK,

@@ -797,7 +797,8 @@ static int pf_launch_gemm(const PfMaps& maps, const PfArgs& a, const DeviceInfo*
     if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "prefill gemm smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev->device] = true;
   }
-  pf_gemm_kernel<MODE><<<dev->sm_count, kPfThreads, smem, st>>>(maps, a);
+  const int grid = dev->pf_ctas > 0 && dev->pf_ctas < dev->sm_count ? dev->pf_ctas : dev->sm_count;
+  pf_gemm_kernel<MODE><<<grid, kPfThreads, smem, st>>>(maps, a);
   return check_launch(MODE == kGateUp ? "pf_gemm<gate/up>" : "pf_gemm<down>");
 }
 
@@ -919,6 +920,15 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_moe_prefill: memset: %s", cudaGetErrorString(e));
   a.pair_ex = pair_eh;
   return pf_launch_gemm<kDown>(dn_maps, a, dev, st);
+}
+
+extern "C" int qfn_set_prefill_sm_budget(int n_sms) {
+  QFN_REQUIRE(n_sms >= 0, QFN_ERR_INVALID_ARG, "qfn_set_prefill_sm_budget: n_sms=%d", n_sms);
+  DeviceInfo* dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  dev->pf_ctas = n_sms;
+  return QFN_OK;
 }
 
 extern "C" int qfn_prefill_status(unsigned int* status, int clear) {

@@ -166,29 +166,48 @@ def moe_prefill_ep(x, ti, tv, table, s2, L, shard, group=None, compute=None):
     return out
 
 
-def moe_prefill_ep_ag(x, ti, tv, table, s2, L, shard, group=None, compute=None):
+def moe_prefill_ep_ag(x, ti, tv, table, s2, L, shard, group=None, compute=None, chunks=1):
     """Expert-parallel MoE layer through all-gather + reduce-scatter (no host sync).
 
     Arguments as moe_prefill_ep; every rank passes the same number of tokens T.
     `compute(x_all, ti_local [N*T, topk] (-1 = another rank's expert), tv_all,
     table, s2, L)` defaults to qmoe.moe_prefill.
-    """
+
+    chunks > 1 pipelines the layer over that many slices of the tokens: every
+    all-gather is queued first, then each slice's grouped GEMM runs as soon as
+    its gather has landed and its reduce-scatter is queued behind it, so the
+    NCCL stream carries one slice's exchange while the compute stream runs
+    another slice's GEMMs (the GEMMs leave SMs for NCCL's kernels when the
+    caller has set a prefill SM budget, _lib.set_prefill_sm_budget)."""
     compute = compute or qmoe.moe_prefill
     N = shard.world
     T, K = ti.shape
     dev = x.device
-    x_all = torch.empty(N * T, x.shape[1], dtype=x.dtype, device=dev)
-    dist.all_gather_into_tensor(x_all, x.contiguous(), group=group)
-    meta = torch.cat([ti.to(torch.int32), tv.float().contiguous().view(torch.int32)], 1).contiguous()
-    meta_all = torch.empty(N * T, 2 * K, dtype=torch.int32, device=dev)
-    dist.all_gather_into_tensor(meta_all, meta, group=group)
-    ti_loc = shard.maps(dev)[2][meta_all[:, :K].long()]        # this rank's local index, -1 elsewhere
-    tv_all = meta_all[:, K:].contiguous().view(torch.float32)
-    y_all = compute(x_all, ti_loc, tv_all, table, s2, L)
+    gloo = dist.get_backend(group) == "gloo"      # gloo has no reduce_scatter_tensor
+    mine = shard.maps(dev)[2]
+    bounds = [T * c // max(chunks, 1) for c in range(max(chunks, 1) + 1)]
+    pending = []
+    for c in range(len(bounds) - 1):              # queue every all-gather first
+        a, b = bounds[c], bounds[c + 1]
+        x_all = torch.empty(N * (b - a), x.shape[1], dtype=x.dtype, device=dev)
+        meta = torch.cat([ti[a:b].to(torch.int32), tv[a:b].float().contiguous().view(torch.int32)], 1).contiguous()
+        meta_all = torch.empty(N * (b - a), 2 * K, dtype=torch.int32, device=dev)
+        w1 = dist.all_gather_into_tensor(x_all, x[a:b].contiguous(), group=group, async_op=True)
+        w2 = dist.all_gather_into_tensor(meta_all, meta, group=group, async_op=True)
+        pending.append((a, b, x_all, meta_all, meta, w1, w2))
     out = torch.empty(T, x.shape[1], dtype=torch.float32, device=dev)
-    if dist.get_backend(group) == "gloo":          # gloo has no reduce_scatter_tensor
-        dist.all_reduce(y_all, group=group)
-        out.copy_(y_all[shard.rank * T:(shard.rank + 1) * T])
-    else:
-        dist.reduce_scatter_tensor(out, y_all, group=group)
+    scatters = []
+    for a, b, x_all, meta_all, meta, w1, w2 in pending:
+        w1.wait()                                 # the compute stream waits for the gather (no host wait)
+        w2.wait()
+        ti_loc = mine[meta_all[:, :K].long()]     # this rank's local index, -1 elsewhere
+        tv_all = meta_all[:, K:].contiguous().view(torch.float32)
+        y_all = compute(x_all, ti_loc, tv_all, table, s2, L)
+        if gloo:
+            dist.all_reduce(y_all, group=group)
+            out[a:b].copy_(y_all[shard.rank * (b - a):(shard.rank + 1) * (b - a)])
+        else:
+            scatters.append((dist.reduce_scatter_tensor(out[a:b], y_all, group=group, async_op=True), y_all))
+    for w, _ in scatters:
+        w.wait()
     return out

@@ -104,6 +104,7 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert dn(4, 3, 128, 128) == 1
     assert dn(4, 2, 96, 128) == 4
     assert dn(4, 2, 128, 100) == 4
+    assert lib.qfn_set_prefill_sm_budget(-1) == 1
 
 
 def test_python_wrappers_reject_cpu_tensors():

@@ -65,6 +65,8 @@ def _worker(rank, port, results, mode="a2a", placement="contiguous"):
         own = shard.experts
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
         fn, compute = (ep.moe_prefill_ep, _cpu_compute) if mode == "a2a" else (ep.moe_prefill_ep_ag, _cpu_compute_ag)
+        if mode == "ag2":    # the all-gather exchange pipelined over two slices of the tokens
+            fn = lambda *a, **k: ep.moe_prefill_ep_ag(*a, chunks=2, **k)
         out = fn(torch.from_numpy(x[toks]), torch.from_numpy(ti[toks]).long(), torch.from_numpy(tv[toks]),
                  torch.from_numpy(blocks[own]), torch.from_numpy(s2[own]), 0, shard, compute=compute)
         results[rank] = out.numpy()
@@ -73,9 +75,10 @@ def _worker(rank, port, results, mode="a2a", placement="contiguous"):
 
 
 @pytest.mark.parametrize("placement", ["contiguous", "lpt"])
-@pytest.mark.parametrize("mode", ["a2a", "ag"])
+@pytest.mark.parametrize("mode", ["a2a", "ag", "ag2"])
 def test_expert_parallel_prefill_matches_single_process(mode, placement):
-    """mode a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter.
+    """mode a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter;
+    ag2: the same pipelined over two slices of the tokens.
     placement: contiguous ranges or the load-aware (LPT) placement."""
     blocks, s2, x, ti, tv = _inputs()
     # both ranks really exchange: some pairs of each rank's tokens live on the other rank

@@ -47,6 +47,10 @@ def _worker(rank, port, results, mode="a2a"):
         own = shard.experts
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
         fn = ep.moe_prefill_ep if mode == "a2a" else ep.moe_prefill_ep_ag
+        if mode == "ag2":    # pipelined over two slices of the tokens, GEMMs on 132 SMs
+            import _lib
+            _lib.set_prefill_sm_budget(132)
+            fn = lambda *a, **k: ep.moe_prefill_ep_ag(*a, chunks=2, **k)
         out = fn(x[toks].to(dev), torch.from_numpy(ti[toks]).long().to(dev),
                  torch.from_numpy(tv[toks]).to(dev).to(torch.bfloat16),
                  torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0, shard)
@@ -58,7 +62,7 @@ def _worker(rank, port, results, mode="a2a"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["a2a", "ag"])
+@pytest.mark.parametrize("mode", ["a2a", "ag", "ag2"])
 def test_expert_parallel_prefill_two_gpus_matches_oracle(mode):
     """a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter (pairs of
     the other rank's experts passed to the grouped GEMM as -1)."""
