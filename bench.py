@@ -81,7 +81,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="qfn", choices=["qfn", "reference"])
     p.add_argument("--workload", default="prefill",
-                   choices=["prefill", "decode", "gemv", "batch-decode", "fp8-linear"],
+                   choices=["prefill", "decode", "gemv", "batch-decode", "fp8-linear", "decode-block", "deltanet"],
                    help="prefill: config 3, the headline (with sub-records); the others print one record alone")
     p.add_argument("--no-sub", action="store_true", help="headline only, no sub-records")
     p.add_argument("--sub-steps", type=int, default=64, help="timed steps of each sub-record")
@@ -93,7 +93,7 @@ def parse():
     p.add_argument("--ep-mode", default="ag", choices=["ag", "a2a"],
                    help="expert-parallel exchange: ag = all-gather + reduce-scatter (no host sync), "
                         "a2a = all-to-all of routed rows (host sync for split sizes)")
-    p.add_argument("--ep-chunks", type=int, default=2,
+    p.add_argument("--ep-chunks", type=int, default=1,
                    help="ag exchange: token slices pipelined so one slice's exchange overlaps another's GEMMs")
     p.add_argument("--ep-sm-budget", type=int, default=-16,
                    help="SMs for the persistent prefill GEMMs under expert parallelism with --ep-chunks > 1 "
@@ -908,6 +908,171 @@ def batch_decode_record(ctx, steps):
     return rec
 
 
+# ---------------------------------------------------------------- the decode MoE block
+SH_INTER = 640      # shared-expert width: the checkpoint's config.json is absent here; the routed experts' 640 assumed
+BLOCK_METRIC = "decode MoE block us/layer (router + 10 routed NVFP4 experts + bf16 shared expert, 48 layers)"
+
+
+def decode_block_record(ctx, steps):
+    """The whole T == 1 MoE block of QwenEngine.moe (qwen_engine.py:801-829) on the
+    device: fused router (bf16 [512, 2560], N(0, 0.02)) -> routed experts on the
+    48-layer table -> bf16 shared expert + combine; 48 layers in one CUDA graph,
+    nothing read back to the host between layers."""
+    import numpy as np
+    import torch
+    import moe_block
+    import routing
+    args, dev = ctx.args, ctx.dev
+    table = ctx.table48()
+    L = args.n_layers
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 41)
+    routers = [(torch.randn(N_EXPERTS, HID, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(L)]
+    shared = [tuple((torch.randn(*shp, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+                    for shp in ((SH_INTER, HID), (SH_INTER, HID), (HID, SH_INTER), (1, HID))) for _ in range(L)]
+    xs = [torch.randn(1, HID, device=dev, generator=g).to(torch.bfloat16) for _ in range(L)]
+    blk = moe_block.DecodeMoE(table, topk=TOPK)
+    outs = [torch.empty(1, HID, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+
+    def step():
+        for l in range(L):
+            blk(xs[l], l, routers[l], *shared[l], out=outs[l])
+
+    step()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    ms, clk = ctx.timed(lambda i: gr.replay(), steps, args.warmup, clocks=True)
+    layer_bytes = LAYER_BYTES + N_EXPERTS * HID * 2 + 3 * SH_INTER * HID * 2 + HID * 2
+    # parity: the last layer's block against the oracle on the kernel's routing
+    oracle = oracle_mod(host_threads(ctx))
+    l = L - 1
+    blk(xs[l], l, routers[l], *shared[l], out=outs[l])
+    torch.cuda.synchronize()
+    r = blk.route_buf
+    ti = r["ti"][0].cpu().numpy()
+    logits = r["logits"].float().cpu().numpy()
+    ti_ref, coef_ref = oracle.route(logits, TOPK)
+    route_ok = bool(np.array_equal(ti, ti_ref[0]))
+    blocks = table.slots[torch.from_numpy(ti + l * N_EXPERTS).long().to(dev)].cpu().numpy()
+    y = oracle.moe_decode(blocks, np.arange(TOPK, dtype=np.int32), table.s2[l][torch.from_numpy(ti).long()].cpu().numpy(),
+                          r["tv"][0].float().cpu().numpy(), xs[l].float().cpu().numpy()[0])
+    ref = oracle.shared_expert(*(t.float().cpu().numpy() for t in (xs[l],) + shared[l]), y[None])
+    got = outs[l].float().cpu().numpy()
+    parity = ctx.parity([rel_err(got, ref)], route_ok and int(got.argmax()) == int(ref.argmax()), 1)
+    parity["tol"] = 1e-2
+    parity["pass"] = parity["max_err_rms"] <= 1e-2 and parity["argmax_equal"]
+    parity["checker"] = "oracle router + moe_decode + shared expert (bf16 output: a few bf16 steps)"
+
+    # e2e: x of every layer from pinned host memory, every layer's bf16 output back, one graph
+    h_x = torch.stack(xs).cpu().pin_memory()
+    h_out = torch.empty(L, 1, HID, dtype=torch.bfloat16).pin_memory()
+    d_x = torch.stack(xs)
+
+    def e2e_step(i):
+        d_x.copy_(h_x, non_blocking=True)
+        for l_ in range(L):
+            xs[l_].copy_(d_x[l_])
+        gr.replay()
+        h_out.copy_(torch.stack(outs), non_blocking=True)
+
+    ms_e2e = ctx.timed(e2e_step, min(args.e2e_steps, steps), 2)
+    hbm, _, kind = peaks()
+    achieved = layer_bytes * L / (ms * 1e-3) / 1e9
+    if not parity["pass"]:
+        ctx.failed.append("decode-block")
+    del gr
+    return {
+        "metric": BLOCK_METRIC, "value": ms * 1e3 / L, "unit": "us/layer", "higher_is_better": False,
+        "ms_per_step": ms, "steps": steps,
+        "config": {"workload": f"decode MoE block x {L} layers (bs=1): router bf16 [512, 2560], top-{TOPK} of 512 "
+                               f"(routing from the router's logits), shared expert bf16 [{SH_INTER}, 2560] x 3 "
+                               f"(width assumed: no config.json here)", "layer_bytes": layer_bytes,
+                   "l2": "no flush: each step streams > 1.3 GB of distinct expert bytes (> 126 MB L2)"},
+        "e2e": {"value": ms_e2e * 1e3 / L, "unit": "us/layer", "h2d_bytes_per_step": L * HID * 2,
+                "d2h_bytes_per_step": L * HID * 2, "ms_per_step": ms_e2e,
+                "path": "moe_block.DecodeMoE per layer (router, routed experts, shared expert) in one CUDA graph; "
+                        "x in from and bf16 outputs out to pinned host memory"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None,
+                     "kernel": "moe_route_logits + moe_route_select + moe_decode_slice + shared_gate_up + shared_down"},
+        "parity": parity,
+        "gpu_launches": steps * L * 5,
+        "clocks": clk,
+    }
+
+
+DN_HEADS, DN_KEY_HEADS, DN_DK, DN_DV, DN_LAYERS = 32, 32, 128, 128, 36   # from the config-1 GEMV shapes
+
+
+def deltanet_record(ctx, steps):
+    """One decoded token through the DeltaNet state updates of 36 linear-attention
+    layers (qwen_engine.py:718-719): 32 value heads, dk = dv = 128 (the shapes the
+    config-1 GEMVs imply: qkv 12288 = 2 x 32 x 128 + 32 x 128, out K = 4096),
+    state 2 MB per layer read and written once; one CUDA graph per step."""
+    import numpy as np
+    import torch
+    import deltanet
+    import synthetic
+    args, dev = ctx.args, ctx.dev
+    H, Hk, dk, dv, L = DN_HEADS, DN_KEY_HEADS, DN_DK, DN_DV, DN_LAYERS
+    q, k, v, g, beta, S0 = synthetic.deltanet_inputs(L, H, Hk, dk, dv, seed=args.seed + 51)
+    q, k, v, g, beta = (t.to(dev) for t in (q, k, v, g, beta))
+    S = [S0[None].clone().to(dev) for _ in range(L)]
+    outs = []
+
+    def step():
+        outs.clear()
+        for l in range(L):
+            o, _ = deltanet.recurrent_gated_delta_rule(q[l][None, None], k[l][None, None], v[l][None, None],
+                                                       g[l][None, None], beta[l][None, None], S[l])
+            outs.append(o)
+
+    step()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    ms, clk = ctx.timed(lambda i: gr.replay(), steps, args.warmup, clocks=True)
+    state_bytes = 2 * H * dk * dv * 4
+    layer_bytes = state_bytes + (2 * Hk * dk + H * dv) * 2 + H * 6 + H * dv * 2
+    # parity: one step of layer 0 from a known state against the fp64 oracle
+    oracle = oracle_mod(host_threads(ctx))
+    S_ref = S0.double().numpy().copy()
+    S_k = S0[None].clone().to(dev)
+    o, _ = deltanet.recurrent_gated_delta_rule(q[0][None, None], k[0][None, None], v[0][None, None],
+                                               g[0][None, None], beta[0][None, None], S_k)
+    ref = oracle.deltanet_step(q[0].float().cpu().numpy(), k[0].float().cpu().numpy(), v[0].float().cpu().numpy(),
+                               g[0].cpu().numpy(), beta[0].float().cpu().numpy(), S_ref)
+    s_err = float(np.abs(S_k[0].cpu().numpy() - S_ref).max() / np.sqrt(np.mean(S_ref ** 2)))
+    got = np.ascontiguousarray(o[0, 0].float().cpu().numpy())
+    steps_ = np.abs((got.view(np.int32) >> 16).astype(np.int64) - (ref.view(np.int32) >> 16).astype(np.int64))
+    parity = ctx.parity([s_err], bool(steps_.max() <= 1), 1)
+    parity["tol"] = 1e-5
+    parity["pass"] = parity["max_err_rms"] <= 1e-5 and parity["argmax_equal"]
+    parity["checker"] = ("oracle.deltanet_step (fp64): fp32 state within 1e-5 of RMS (max_err_rms); every bf16 "
+                         "output within one bf16 step (argmax_equal)")
+    hbm, _, kind = peaks()
+    achieved = layer_bytes * L / (ms * 1e-3) / 1e9
+    if not parity["pass"]:
+        ctx.failed.append("deltanet")
+    del gr
+    return {
+        "metric": "DeltaNet one-token state update us/layer (32 heads, 128 x 128 fp32 state)", "value": ms * 1e3 / L,
+        "unit": "us/layer", "higher_is_better": False, "ms_per_step": ms, "steps": steps,
+        "config": {"workload": f"{L} linear-attention layers x one token; heads {H} (key heads {Hk}), dk {dk}, "
+                               f"dv {dv}; one CUDA graph per step", "layer_bytes": layer_bytes,
+                   "l2": f"no flush: {L} states of {state_bytes / 2 / 1e6:.1f} MB = {L * state_bytes / 2e6:.0f} MB "
+                         "per step (> 126 MB L2 with reads and writes)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind, "traffic": None, "kernel": "deltanet_step_kernel"},
+        "parity": parity,
+        "gpu_launches": steps * L,
+        "clocks": clk,
+    }
+
+
 # ---------------------------------------------------------------- FP8 linear layer for T > 1
 def fp8_linear_record(ctx, steps):
     """The engine's FP8 linear layer for T > 1 tokens (Lin.__call__, qwen_engine.py:79-83):
@@ -1085,11 +1250,14 @@ def main():
             if ctx.world == 1:
                 subs["decode_config2"] = decode_record(ctx, max(sub_steps, 4))
                 subs["gemv_config1"] = gemv_record(ctx, max(sub_steps, 4))
+                subs["decode_moe_block"] = decode_block_record(ctx, max(sub_steps // 2, 4))
+                subs["deltanet_step"] = deltanet_record(ctx, max(sub_steps, 4))
             subs["batch_decode_config4"] = batch_decode_record(ctx, max(sub_steps // 4, 4))
             line["sub"] = subs
     else:
         fn = {"decode": decode_record, "gemv": gemv_record, "batch-decode": batch_decode_record,
-              "fp8-linear": fp8_linear_record}[args.workload]
+              "fp8-linear": fp8_linear_record, "decode-block": decode_block_record,
+              "deltanet": deltanet_record}[args.workload]
         line = fn(ctx, args.steps)
         line.setdefault("n_gpus", ctx.world)
         line.setdefault("warmup", max(args.warmup, 3))

@@ -199,7 +199,7 @@ int qfn_moe_route(const uint16_t* x, const uint16_t* w_router, int64_t T, int n_
  *   16-byte aligned.  y: f32[T][2560] device or NULL.
  *   h: bf16[T][inter] device scratch (holds silu(g) * u on return), 16-byte
  *   aligned; gt: bf16[T] device scratch (the gate); out: bf16[T][2560].
- *   inter % 256 == 0, 256 <= inter <= 4096; 1 <= T <= 4096.
+ *   inter % 8 == 0, 8 <= inter <= 4096; 1 <= T <= 4096.
  *   Two launches (gate/up, then down as a programmatic dependent); both read
  *   their weight rows before the dependency wait, so nothing earlier in the
  *   stream may write the weights while they run.

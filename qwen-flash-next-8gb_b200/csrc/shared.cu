@@ -168,8 +168,8 @@ extern "C" int qfn_shared_expert(const uint16_t* x, int64_t T, const uint16_t* w
   QFN_REQUIRE(x && w_gate && w_up && w_down && w_sg && h && gt && out, QFN_ERR_INVALID_ARG,
               "qfn_shared_expert: null pointer");
   QFN_REQUIRE(T >= 1 && T <= 4096, QFN_ERR_UNSUPPORTED, "qfn_shared_expert: T=%lld outside [1, 4096]", (long long)T);
-  QFN_REQUIRE(inter >= 256 && inter <= kShMaxInter && inter % 256 == 0, QFN_ERR_UNSUPPORTED,
-              "qfn_shared_expert: inter=%d must be a multiple of 256 in [256, %d]", inter, kShMaxInter);
+  QFN_REQUIRE(inter >= 8 && inter <= kShMaxInter && inter % 8 == 0, QFN_ERR_UNSUPPORTED,
+              "qfn_shared_expert: inter=%d must be a multiple of 8 in [8, %d]", inter, kShMaxInter);
   QFN_REQUIRE(aligned(x, 16) && aligned(w_gate, 16) && aligned(w_up, 16) && aligned(w_down, 16) && aligned(w_sg, 16) &&
                   aligned(h, 16),
               QFN_ERR_ALIGNMENT, "qfn_shared_expert: x, weights and h must be 16-byte aligned");

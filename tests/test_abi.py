@@ -95,7 +95,7 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     # shared expert: nulls, inter % 256 and range, alignment
     sh = lambda x, I: lib.qfn_shared_expert(x, 1, fake, fake, fake, fake, I, None, fake, fake, fake, None)
     assert sh(None, 512) == 1
-    assert sh(fake, 320) == 4
+    assert sh(fake, 644) == 4
     assert sh(fake, 8192) == 4
     assert sh(odd, 512) == 2
     # delta rule: nulls, head ratio, dk / dv
