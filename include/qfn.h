@@ -234,9 +234,6 @@ int qfn_deltanet_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, c
  *   s: f32[N] device; x: bf16[K] device (raw 16-bit words).
  *   y: [N] device, y_dtype QFN_DTYPE_BF16 (the reference's output, rounded to
  *      nearest even) or QFN_DTYPE_F32 (the unrounded accumulator * s).
- *   q and s are parameters: the kernel starts reading q before it waits for
- *   the previous kernel in the stream, so no earlier kernel of the stream may
- *   still be writing them (x may be).
  */
 int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
                   int y_dtype, int64_t N, int64_t K, qfn_stream_t stream);

@@ -194,18 +194,17 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     mbar_arrive_expect_tx(&full[i % S], bytes);
     bulk_g2s(sm + L.ring + (i % S) * 16 * K, q + row0 * K, bytes, &full[i % S]);
   };
-  // The weights and row scales are parameters that no kernel of the engine
-  // writes (the precondition of this entry point): the first ring of weight
-  // tiles is requested before the dependency wait, so it streams during the
-  // previous kernel's tail.  x may come from the previous kernel in the
-  // stream: it is copied only after the wait.
-  if (threadIdx.x == 0)
-    for (int i = 0; i < nt && i < S; ++i) issue(i);
+  // Inputs may come from the previous kernel in the stream: wait for it (the
+  // launch and the prologue above overlap its tail).  Requesting the weight
+  // tiles before the wait measured no faster: at 225 KB of shared memory the
+  // next call's CTAs become resident only as this call's leave.
   pdl_wait();
   pdl_launch_dependents();
+  // x first (ordinary loads would queue behind the weight stream), then the tiles.
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(&full[8], 2 * K);
     bulk_g2s(sm + L.xraw, x, 2 * K, &full[8]);
+    for (int i = 0; i < nt && i < S; ++i) issue(i);
   }
 
   // x -> f16 hi/lo * 2^ex (thread u owns k = u, u + 512, ...)

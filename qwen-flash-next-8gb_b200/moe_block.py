@@ -66,14 +66,29 @@ class DecodeMoE:
             "coef": torch.empty(T, topk, dtype=torch.float32, device=dev),
             "s2": torch.empty(T, topk, 3, dtype=torch.float32, device=dev),
         }
+        self.side = None
         self.h_buf = torch.empty(topk, 640, dtype=torch.float32, device=dev)
         self.o_buf = torch.empty(topk, 2560, dtype=torch.float32, device=dev)
 
     def __call__(self, x, layer, router, w_gate, w_up, w_down, w_sg, out=None):
         """x bf16 [1, 2560] (the MoE input of one token) -> bf16 [1, 2560] =
-        moe_decode(routed experts).to(bf16) + shared expert (qwen_engine.py:801-829)."""
+        moe_decode(routed experts).to(bf16) + shared expert (qwen_engine.py:801-829).
+
+        The shared expert does not depend on the routing: it runs on a side
+        stream while the router and the routed experts run on the caller's
+        stream, and the two meet in the reference's own combine,
+        y.to(bf16) + sh (qwen_engine.py:829)."""
         if x.dim() != 2 or x.shape[0] != 1:
             raise ValueError("DecodeMoE takes one token: x [1, 2560]")
+        cur = torch.cuda.current_stream(x.device)
+        if self.side is None:
+            self.side = torch.cuda.Stream(x.device)
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            sh = shared_expert(x, w_gate, w_up, w_down, w_sg)
         r = routing.route_fused(x, router, self.topk, layer, self.table.s2, out=self.route_buf)
         y = qmoe.moe_decode(self.table.slots, r["sidx"][0], r["s2"][0], r["coef"][0], x[0], self.h_buf, self.o_buf)
-        return shared_expert(x, w_gate, w_up, w_down, w_sg, y=y, out=out)
+        cur.wait_stream(self.side)
+        sh.record_stream(cur)
+        res = torch.add(y.to(torch.bfloat16)[None], sh, out=out)
+        return res
