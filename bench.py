@@ -67,9 +67,13 @@ LIN_COPIES = 4
 # DRAM bytes (read + written) per launch of the dominant kernel of each
 # record, from ncu captures of the same shapes (None: not captured).
 TRAFFIC = {
-    "decode": 27.74e6,              # moe_decode_slice, one layer (K = 10)
-    "prefill": 1.767e9,             # pf_gemm<0> + pf_gemm<1>, one config-3 layer
-    "gemv_ratio": 10.55e6 / 10.509312e6,   # gemv_stream_kernel DRAM bytes / algorithmic bytes
+    "decode": 27.72e6,              # moe_decode_slice, one layer (K = 10)
+    "prefill": 1.7508e9,            # pf_gemm<0> + pf_gemm<1>, one config-3 layer
+    "gemv_ratio": 31.554816e6 / 31.536128e6,   # gemv_stream_kernel (12288 x 2560) DRAM bytes / algorithmic bytes
+    # route logits + select + moe_decode_slice + shared gate/up + down, one layer
+    "decode_block": 2.635e6 + 0.064e6 + 27.72e6 + 6.581e6 + 3.289e6,
+    # deltanet_step_kernel: the state's reads (its writes reach DRAM from L2 after the launch)
+    "deltanet": 2.140e6,
 }
 PARITY_TOL = 1e-3       # north_star: max |err| <= 1e-3 x RMS of the oracle's output
 
@@ -995,7 +999,7 @@ def decode_block_record(ctx, steps):
                 "path": "moe_block.DecodeMoE per layer (router, routed experts, shared expert) in one CUDA graph; "
                         "x in from and bf16 outputs out to pinned host memory"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None,
+                     "peak_kind": kind, "traffic": TRAFFIC["decode_block"],
                      "kernel": "moe_route_logits + moe_route_select + moe_decode_slice + shared_gate_up + shared_down"},
         "parity": parity,
         "gpu_launches": steps * L * 5,
@@ -1066,7 +1070,7 @@ def deltanet_record(ctx, steps):
                    "l2": f"no flush: {L} states of {state_bytes / 2 / 1e6:.1f} MB = {L * state_bytes / 2e6:.0f} MB "
                          "per step (> 126 MB L2 with reads and writes)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": kind, "traffic": None, "kernel": "deltanet_step_kernel"},
+                     "peak_kind": kind, "traffic": TRAFFIC["deltanet"], "kernel": "deltanet_step_kernel"},
         "parity": parity,
         "gpu_launches": steps * L,
         "clocks": clk,

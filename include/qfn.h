@@ -209,6 +209,23 @@ int qfn_shared_expert(const uint16_t* x, int64_t T, const uint16_t* w_gate, cons
                       uint16_t* h, uint16_t* gt, uint16_t* out, qfn_stream_t stream);
 
 /*
+ * The two halves of qfn_shared_expert as separate launches, so that the
+ * gate/up half (which does not depend on the routing) can run on another
+ * stream while the router and the routed experts run, and the down half can
+ * follow the routed experts and fuse the combine with their output y:
+ *   qfn_shared_expert_gate_up: h = bf16(silu(w_gate . x)) * (w_up . x) rounded
+ *     as above, gt = bf16(sigmoid(bf16(x . w_sg)));
+ *   qfn_shared_expert_down: out = bf16(y) + bf16(gt * bf16(w_down . h)), or
+ *     the shared term alone when y is NULL.
+ * Same arguments, shapes, alignment and limits as qfn_shared_expert.
+ * qfn_shared_expert = gate_up then down on one stream.
+ */
+int qfn_shared_expert_gate_up(const uint16_t* x, int64_t T, const uint16_t* w_gate, const uint16_t* w_up,
+                              const uint16_t* w_sg, int inter, uint16_t* h, uint16_t* gt, qfn_stream_t stream);
+int qfn_shared_expert_down(const uint16_t* w_down, int inter, int64_t T, const uint16_t* h, const uint16_t* gt,
+                           const float* y, uint16_t* out, qfn_stream_t stream);
+
+/*
  * qfn_deltanet_step -- replaces recurrent_gated_delta_rule at T == 1
  * (qwen_engine.py:158-174), the per-token state update of the DeltaNet
  * layers (QwenEngine.deltanet, qwen_engine.py:718-719):

@@ -36,6 +36,8 @@ SIGNATURES = {
     "qfn_set_prefill_sm_budget": [_I],
     "qfn_moe_route": [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "qfn_shared_expert": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
+    "qfn_shared_expert_gate_up": [_P, _I64, _P, _P, _P, _I, _P, _P, _P],
+    "qfn_shared_expert_down": [_P, _I, _I64, _P, _P, _P, _P, _P],
     "qfn_deltanet_step": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
 }
 # entry points whose return value is not an int status

@@ -19,9 +19,12 @@
 // the previous kernel's tail) and multiplies them with the T token rows
 // (staged 8 at a time in shared memory): the 2.6 MB of router weights stream
 // from HBM once, spread over E / 4 CTAs.  Select (a programmatic dependent of
-// the logits kernel): one warp per token: max, exp, sum and division as
-// torch's softmax does them in fp32, then k rounds of a warp argmax
-// (probability, then lower index), the renormalisation summed in rank order.
+// the logits kernel): one 256-thread CTA per token: max, exp, sum and
+// division as torch's softmax does them in fp32; then each warp takes the
+// top k of its experts by k rounds of a 64-bit warp arg-max (probability,
+// then lower index: two 32-bit redux.sync reductions a round), and warp 0
+// the top k of the warps' candidates the same way; the renormalisation is
+// summed in rank order.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -34,6 +37,7 @@ constexpr int kRtTok = 8;                        // token rows staged in shared 
 constexpr int kRtChunks = kHid / 8 / 32;         // 16-byte chunks of a row per lane: 10
 constexpr int kRtMaxExperts = 1024;              // <= 32 logits per lane in phase 2
 constexpr int kRtMaxTopk = 32;
+constexpr int kSelThreads = 256;                // selection: one CTA per token
 
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
   const __nv_bfloat16 b = __float2bfloat16_rn(v);
@@ -80,75 +84,110 @@ __global__ void __launch_bounds__(32 * kRtWarps) moe_route_logits_kernel(const u
   }
 }
 
-__global__ void __launch_bounds__(32 * kRtWarps) moe_route_select_kernel(
+// Selection keys: probability bits (p >= 0, so the bits order as the values)
+// above the complement of the expert id, so that of equal probabilities the
+// lower id is the larger key; 0 = no comparable probability (NaN) or taken.
+__device__ __forceinline__ uint64_t sel_key(float p, int e) {
+  return p == p ? (static_cast<uint64_t>(__float_as_uint(p)) << 32) | (0xffffffffu - static_cast<uint32_t>(e)) : 0ull;
+}
+
+// The largest 64-bit key of the warp, from two 32-bit warp reductions.
+__device__ __forceinline__ uint64_t warp_max_key(uint64_t k) {
+  const uint32_t hi = __reduce_max_sync(0xffffffffu, static_cast<uint32_t>(k >> 32));
+  const uint32_t lo = __reduce_max_sync(0xffffffffu, static_cast<uint32_t>(k >> 32) == hi ? static_cast<uint32_t>(k) : 0u);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+// k rounds of a warp arg-max over the keys the lanes hold (kN each); lane r
+// returns the r-th largest key (0 once none is left).
+template <int kN>
+__device__ __forceinline__ uint64_t warp_topk(uint64_t (&key)[kN], int topk, int lane) {
+  uint64_t best = 0, mine = 0;
+#pragma unroll
+  for (int j = 0; j < kN; ++j) best = key[j] > best ? key[j] : best;
+  for (int r = 0; r < topk; ++r) {
+    const uint64_t w = warp_max_key(best);
+    if (lane == r) mine = w;
+    if (w != 0 && best == w) {   // the one lane holding the winner takes it out of the race
+      best = 0;
+#pragma unroll
+      for (int j = 0; j < kN; ++j) {
+        if (key[j] == w) key[j] = 0;
+        best = key[j] > best ? key[j] : best;
+      }
+    }
+  }
+  return mine;
+}
+
+__global__ void __launch_bounds__(kSelThreads) moe_route_select_kernel(
     const uint16_t* __restrict__ logits, int T, int E, int topk, int64_t sidx_base, const float* __restrict__ s2_layer,
     int32_t* __restrict__ ti, uint16_t* __restrict__ tv, int32_t* __restrict__ sidx, float* __restrict__ coef,
     float* __restrict__ s2_out) {
+  constexpr int kW = kSelThreads / 32;
+  constexpr int kPer = kRtMaxExperts / kSelThreads;   // experts per thread
+  __shared__ float red[kW];
+  __shared__ uint64_t cand[kW][kRtMaxTopk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kRtWarps + warp;
+  const int t = blockIdx.x;
   pdl_wait();                 // the logits kernel has finished
   pdl_launch_dependents();
-  if (t >= T) return;         // warp-uniform
-  const int per = (E + 31) / 32;
   const uint16_t* lg = logits + static_cast<int64_t>(t) * E;
-  float p[kRtMaxExperts / 32];
+  float p[kPer];
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kRtMaxExperts / 32; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = (j < per && e < E) ? bf16_bits_to_f32(__ldcg(lg + e)) : -INFINITY;
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x + kSelThreads * j;
+    p[j] = e < E ? bf16_bits_to_f32(__ldcg(lg + e)) : -INFINITY;
     mx = fmaxf(mx, p[j]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kW; ++w) mx = fmaxf(mx, red[w]);
   float sum = 0.f;
 #pragma unroll
-  for (int j = 0; j < kRtMaxExperts / 32; ++j) {
+  for (int j = 0; j < kPer; ++j) {
     // exp in double, rounded once to fp32 (correctly rounded in practice): the
     // closest one value per logit that torch's fp32 exp and the host's can land on
-    p[j] = (j < per && lane + 32 * j < E) ? static_cast<float>(exp(static_cast<double>(p[j] - mx))) : 0.f;
+    const int e = threadIdx.x + kSelThreads * j;
+    p[j] = e < E ? static_cast<float>(exp(static_cast<double>(p[j] - mx))) : 0.f;
     sum += p[j];
   }
   sum = warp_sum(sum);
+  __syncthreads();            // every warp has read red[] as maxima
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = red[0];
 #pragma unroll
-  for (int j = 0; j < kRtMaxExperts / 32; ++j) p[j] = (j < per && lane + 32 * j < E) ? p[j] / sum : -1.f;
-  // top-k: k rounds of a warp argmax over (probability desc, expert id asc)
-  float pk = 0.f;    // lane k keeps the k-th probability and expert
-  int ek = 0;
-  for (int k = 0; k < topk; ++k) {
-    float bv = -1.f;
-    int be = 0x7fffffff;
+  for (int w = 1; w < kW; ++w) sum += red[w];
+  uint64_t key[kPer];
 #pragma unroll
-    for (int j = 0; j < kRtMaxExperts / 32; ++j) {
-      if (p[j] > bv) {   // ascending j: of equal values the lower expert id stays
-        bv = p[j];
-        be = lane + 32 * j;
-      }
-    }
+  for (int j = 0; j < kPer; ++j) {
+    const int e = threadIdx.x + kSelThreads * j;
+    key[j] = e < E ? sel_key(p[j] / sum, e) : 0ull;
+  }
+  // top-k of each warp's experts, then of the warps' candidates (in warp 0)
+  const uint64_t wk = warp_topk<kPer>(key, topk, lane);
+  if (lane < topk) cand[warp][lane] = wk;
+  __syncthreads();
+  if (warp != 0) return;
+  uint64_t ck[kW];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    if (be >= E) {       // no comparable probability left (NaN logits): expert 0, weight NaN
-      be = 0;
-      bv = __int_as_float(0x7fc00000);
-    }
-    if (lane == k) {
-      pk = bv;
-      ek = be;
-    }
-#pragma unroll
-    for (int j = 0; j < kRtMaxExperts / 32; ++j)
-      if (lane + 32 * j == be) p[j] = -2.f;   // the owner takes the winner out of the race
+  for (int w = 0; w < kW; ++w) ck[w] = lane < topk ? cand[w][lane] : 0ull;
+  const uint64_t k = warp_topk<kW>(ck, topk, lane);
+  int ek = 0;                  // no comparable probability left (NaN logits): expert 0, weight NaN
+  float pk = __int_as_float(0x7fc00000);
+  if (k != 0) {
+    ek = static_cast<int>(0xffffffffu - static_cast<uint32_t>(k));
+    pk = __uint_as_float(static_cast<uint32_t>(k >> 32));
   }
   // renormalise: the k probabilities summed in rank order, as the reference's tv.sum(-1)
   float tsum = 0.f;
-  for (int k = 0; k < topk; ++k) tsum += __shfl_sync(0xffffffffu, pk, k);
+  for (int r = 0; r < topk; ++r) tsum += __shfl_sync(0xffffffffu, pk, r);
   if (lane < topk) {
     const int64_t o = static_cast<int64_t>(t) * topk + lane;
     const uint16_t b = f32_to_bf16_bits(pk / tsum);
@@ -196,7 +235,8 @@ extern "C" int qfn_moe_route(const uint16_t* x, const uint16_t* w_router, int64_
   const int Ti = static_cast<int>(T);
   cudaError_t e = cudaLaunchKernelEx(&cfg, moe_route_logits_kernel, x, w_router, Ti, n_experts, logits);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_route_logits_kernel launch: %s", cudaGetErrorString(e));
-  cfg.gridDim = dim3(static_cast<unsigned>((T + kRtWarps - 1) / kRtWarps));
+  cfg.gridDim = dim3(static_cast<unsigned>(T));
+  cfg.blockDim = dim3(kSelThreads);
   e = cudaLaunchKernelEx(&cfg, moe_route_select_kernel, static_cast<const uint16_t*>(logits), Ti, n_experts, topk,
                          sidx_base, s2_layer, ti, tv, sidx, coef, s2_out);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "moe_route_select_kernel launch: %s", cudaGetErrorString(e));

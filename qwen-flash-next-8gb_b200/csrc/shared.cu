@@ -19,7 +19,11 @@
 // 10 KB, in registers; one more warp for the gate row sh_g) writes h and gt;
 // down (a programmatic dependent: a warp per output row) multiplies h into the
 // down rows and applies the gate and the combine.  Token rows are staged in
-// shared memory 8 at a time.
+// shared memory 8 at a time.  The two launches are also entry points of their
+// own (qfn_shared_expert_gate_up, qfn_shared_expert_down): the gate/up half
+// does not depend on the routing and can run on another stream beside the
+// router and the routed experts; the down half then follows the routed
+// experts in their stream and fuses the combine with their output.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -158,41 +162,74 @@ static int launch_shared_down(const cudaLaunchConfig_t& cfg0, const uint16_t* wd
   return check_launch("shared_down_kernel");
 }
 
+static cudaLaunchConfig_t shared_cfg(cudaLaunchAttribute* attr, qfn_stream_t stream, unsigned grid) {
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(32 * kShWarps);
+  cfg.gridDim = dim3(grid);
+  cfg.stream = as_stream(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+static int shared_checks(int64_t T, int inter) {
+  QFN_REQUIRE(T >= 1 && T <= 4096, QFN_ERR_UNSUPPORTED, "qfn_shared_expert: T=%lld outside [1, 4096]", (long long)T);
+  QFN_REQUIRE(inter >= 8 && inter <= kShMaxInter && inter % 8 == 0, QFN_ERR_UNSUPPORTED,
+              "qfn_shared_expert: inter=%d must be a multiple of 8 in [8, %d]", inter, kShMaxInter);
+  return QFN_OK;
+}
+
 }  // namespace qfn
 
 using namespace qfn;
+
+extern "C" int qfn_shared_expert_gate_up(const uint16_t* x, int64_t T, const uint16_t* w_gate, const uint16_t* w_up,
+                                         const uint16_t* w_sg, int inter, uint16_t* h, uint16_t* gt,
+                                         qfn_stream_t stream) {
+  QFN_REQUIRE(x && w_gate && w_up && w_sg && h && gt, QFN_ERR_INVALID_ARG, "qfn_shared_expert: null pointer");
+  int rc = shared_checks(T, inter);
+  if (rc) return rc;
+  QFN_REQUIRE(aligned(x, 16) && aligned(w_gate, 16) && aligned(w_up, 16) && aligned(w_sg, 16) && aligned(h, 16),
+              QFN_ERR_ALIGNMENT, "qfn_shared_expert: x, weights and h must be 16-byte aligned");
+  DeviceInfo* dev;
+  if ((rc = current_device(&dev))) return rc;
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = shared_cfg(attr, stream, (inter + 1 + kShWarps - 1) / kShWarps);   // + the gate row
+  cudaError_t e = cudaLaunchKernelEx(&cfg, shared_gate_up_kernel, x, static_cast<int>(T), w_gate, w_up, w_sg, inter,
+                                     h, gt);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "shared_gate_up_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("shared_gate_up_kernel");
+}
+
+extern "C" int qfn_shared_expert_down(const uint16_t* w_down, int inter, int64_t T, const uint16_t* h,
+                                      const uint16_t* gt, const float* y, uint16_t* out, qfn_stream_t stream) {
+  QFN_REQUIRE(w_down && h && gt && out, QFN_ERR_INVALID_ARG, "qfn_shared_expert: null pointer");
+  int rc = shared_checks(T, inter);
+  if (rc) return rc;
+  QFN_REQUIRE(aligned(w_down, 16) && aligned(h, 16), QFN_ERR_ALIGNMENT,
+              "qfn_shared_expert: weights and h must be 16-byte aligned");
+  DeviceInfo* dev;
+  if ((rc = current_device(&dev))) return rc;
+  cudaLaunchAttribute attr[1];
+  const cudaLaunchConfig_t cfg = shared_cfg(attr, stream, kHid / kShWarps);
+  const int Ti = static_cast<int>(T);
+  if (inter <= 1024) return launch_shared_down<4>(cfg, w_down, inter, Ti, h, gt, y, out);
+  if (inter <= 2048) return launch_shared_down<8>(cfg, w_down, inter, Ti, h, gt, y, out);
+  return launch_shared_down<16>(cfg, w_down, inter, Ti, h, gt, y, out);
+}
 
 extern "C" int qfn_shared_expert(const uint16_t* x, int64_t T, const uint16_t* w_gate, const uint16_t* w_up,
                                  const uint16_t* w_down, const uint16_t* w_sg, int inter, const float* y,
                                  uint16_t* h, uint16_t* gt, uint16_t* out, qfn_stream_t stream) {
   QFN_REQUIRE(x && w_gate && w_up && w_down && w_sg && h && gt && out, QFN_ERR_INVALID_ARG,
               "qfn_shared_expert: null pointer");
-  QFN_REQUIRE(T >= 1 && T <= 4096, QFN_ERR_UNSUPPORTED, "qfn_shared_expert: T=%lld outside [1, 4096]", (long long)T);
-  QFN_REQUIRE(inter >= 8 && inter <= kShMaxInter && inter % 8 == 0, QFN_ERR_UNSUPPORTED,
-              "qfn_shared_expert: inter=%d must be a multiple of 8 in [8, %d]", inter, kShMaxInter);
+  int rc = shared_checks(T, inter);
+  if (rc) return rc;
   QFN_REQUIRE(aligned(x, 16) && aligned(w_gate, 16) && aligned(w_up, 16) && aligned(w_down, 16) && aligned(w_sg, 16) &&
                   aligned(h, 16),
               QFN_ERR_ALIGNMENT, "qfn_shared_expert: x, weights and h must be 16-byte aligned");
-  DeviceInfo* dev;
-  int rc = current_device(&dev);
-  if (rc) return rc;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(32 * kShWarps);
-  cfg.stream = as_stream(stream);
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3((inter + 1 + kShWarps - 1) / kShWarps);   // + the gate row
-  const int Ti = static_cast<int>(T);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, shared_gate_up_kernel, x, Ti, w_gate, w_up, w_sg, inter, h, gt);
-  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "shared_gate_up_kernel launch: %s", cudaGetErrorString(e));
-  if ((rc = check_launch("shared_gate_up_kernel"))) return rc;
-  cfg.gridDim = dim3(kHid / kShWarps);
-  const uint16_t* hc = h;
-  const uint16_t* gc = gt;
-  if (inter <= 1024) return launch_shared_down<4>(cfg, w_down, inter, Ti, hc, gc, y, out);
-  if (inter <= 2048) return launch_shared_down<8>(cfg, w_down, inter, Ti, hc, gc, y, out);
-  return launch_shared_down<16>(cfg, w_down, inter, Ti, hc, gc, y, out);
+  if ((rc = qfn_shared_expert_gate_up(x, T, w_gate, w_up, w_sg, inter, h, gt, stream))) return rc;
+  return qfn_shared_expert_down(w_down, inter, T, h, gt, y, out, stream);
 }

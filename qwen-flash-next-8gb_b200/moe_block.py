@@ -1,8 +1,9 @@
 """The decode MoE block of QwenEngine.moe (qwen_engine.py:801-831) on the device
 with no host synchronisation:
 
-    router (qfn_moe_route) -> routed experts (qfn_moe_decode / qfn_moe_prefill)
-    -> shared expert + combine (qfn_shared_expert)
+    router (qfn_moe_route) -> routed experts (qfn_moe_decode)
+    -> shared expert down + combine (qfn_shared_expert_down)
+    with the shared expert's gate/up (qfn_shared_expert_gate_up) on a side stream
 
 The reference runs the router as torch ops, reads the chosen experts back
 to the host (ti[0].tolist(), qwen_engine.py:812/815) to drive its expert
@@ -69,26 +70,44 @@ class DecodeMoE:
         self.side = None
         self.h_buf = torch.empty(topk, 640, dtype=torch.float32, device=dev)
         self.o_buf = torch.empty(topk, 2560, dtype=torch.float32, device=dev)
+        self.sh_gt = torch.empty(T, dtype=torch.bfloat16, device=dev)
+        self.sh_h = {}
 
     def __call__(self, x, layer, router, w_gate, w_up, w_down, w_sg, out=None):
         """x bf16 [1, 2560] (the MoE input of one token) -> bf16 [1, 2560] =
         moe_decode(routed experts).to(bf16) + shared expert (qwen_engine.py:801-829).
 
-        The shared expert does not depend on the routing: it runs on a side
-        stream while the router and the routed experts run on the caller's
-        stream, and the two meet in the reference's own combine,
-        y.to(bf16) + sh (qwen_engine.py:829)."""
+        The shared expert's gate/up half does not depend on the routing: it
+        runs on a side stream while the router and the routed experts run on
+        the caller's stream.  Its down half follows the routed experts on the
+        caller's stream and applies the reference's combine,
+        y.to(bf16) + sh (qwen_engine.py:829), in the same kernel."""
         if x.dim() != 2 or x.shape[0] != 1:
             raise ValueError("DecodeMoE takes one token: x [1, 2560]")
-        cur = torch.cuda.current_stream(x.device)
+        for name, t in (("x", x), ("w_gate", w_gate), ("w_up", w_up), ("w_down", w_down), ("w_sg", w_sg)):
+            require_cuda(name, t, torch.bfloat16)
+        I = w_gate.shape[0]
+        if tuple(w_gate.shape) != (I, 2560) or tuple(w_up.shape) != (I, 2560) or tuple(w_down.shape) != (2560, I) \
+                or w_sg.numel() != 2560:
+            raise ValueError("shapes: w_gate/w_up [I, 2560], w_down [2560, I], w_sg [1, 2560]")
+        dev = x.device
+        h = self.sh_h.get(I)
+        if h is None:
+            h = self.sh_h[I] = torch.empty(1, I, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(1, 2560, dtype=torch.bfloat16, device=dev) if out is None else out
+        cur = torch.cuda.current_stream(dev)
         if self.side is None:
-            self.side = torch.cuda.Stream(x.device)
+            self.side = torch.cuda.Stream(dev)
         self.side.wait_stream(cur)
-        with torch.cuda.stream(self.side):
-            sh = shared_expert(x, w_gate, w_up, w_down, w_sg)
-        r = routing.route_fused(x, router, self.topk, layer, self.table.s2, out=self.route_buf)
-        y = qmoe.moe_decode(self.table.slots, r["sidx"][0], r["s2"][0], r["coef"][0], x[0], self.h_buf, self.o_buf)
-        cur.wait_stream(self.side)
-        sh.record_stream(cur)
-        res = torch.add(y.to(torch.bfloat16)[None], sh, out=out)
-        return res
+        with on_device(dev):
+            check(lib().qfn_shared_expert_gate_up(x.data_ptr(), 1, w_gate.data_ptr(), w_up.data_ptr(),
+                                                  w_sg.data_ptr(), I, h.data_ptr(), self.sh_gt.data_ptr(),
+                                                  self.side.cuda_stream), "qfn_shared_expert_gate_up")
+            r = routing.route_fused(x, router, self.topk, layer, self.table.s2, out=self.route_buf)
+            y = qmoe.moe_decode(self.table.slots, r["sidx"][0], r["s2"][0], r["coef"][0], x[0], self.h_buf,
+                                self.o_buf)
+            cur.wait_stream(self.side)
+            check(lib().qfn_shared_expert_down(w_down.data_ptr(), I, 1, h.data_ptr(), self.sh_gt.data_ptr(),
+                                               y.data_ptr(), out.data_ptr(), cur.cuda_stream),
+                  "qfn_shared_expert_down")
+        return out

@@ -92,12 +92,20 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert r(fake, 0, 512, 10, None, None) == 4
     assert r(fake, 1, 512, 10, None, fake) == 1
     assert r(odd, 1, 512, 10, None, None) == 2
-    # shared expert: nulls, inter % 256 and range, alignment
+    # shared expert (whole and halves): nulls, inter % 8 and range, T range, alignment
     sh = lambda x, I: lib.qfn_shared_expert(x, 1, fake, fake, fake, fake, I, None, fake, fake, fake, None)
     assert sh(None, 512) == 1
     assert sh(fake, 644) == 4
     assert sh(fake, 8192) == 4
     assert sh(odd, 512) == 2
+    gu = lambda x, I: lib.qfn_shared_expert_gate_up(x, 1, fake, fake, fake, I, fake, fake, None)
+    assert gu(None, 640) == 1
+    assert gu(fake, 644) == 4
+    assert gu(odd, 640) == 2
+    dw = lambda wd, I, T: lib.qfn_shared_expert_down(wd, I, T, fake, fake, None, fake, None)
+    assert dw(None, 640, 1) == 1
+    assert dw(fake, 640, 0) == 4
+    assert dw(odd, 640, 1) == 2
     # delta rule: nulls, head ratio, dk / dv
     dn = lambda H, Hk, dk, dv: lib.qfn_deltanet_step(fake, fake, fake, fake, fake, fake, fake, H, Hk, dk, dv, None)
     assert lib.qfn_deltanet_step(None, fake, fake, fake, fake, fake, fake, 4, 2, 128, 128, None) == 1

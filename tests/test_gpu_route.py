@@ -32,8 +32,12 @@ def bf16(a):
 
 
 def assert_weights_close(a, b):
+    """Router weights within one bf16 step of the oracle's, and rarely off at
+    all: the fp32 sum of the exponentials is summed in another order than the
+    oracle's (as torch's own CUDA softmax is), so a weight whose fp32 value
+    lies next to a bf16 rounding boundary can round the other way."""
     st = bf16_steps(a, b)
-    assert st.max() <= 1 and (st > 0).mean() <= 0.05, (st.max(), (st > 0).mean())
+    assert st.max() <= 1 and (st > 0).sum() <= max(1, 0.05 * st.size), (st.max(), (st > 0).mean())
 
 
 def router_case(T, E, seed, dup_rows=0):
