@@ -132,8 +132,25 @@ namespace qfn {
 // kStatusTimeout in the device status word of the kernel's translation unit
 // and the kernel carries on (its outputs are then garbage; the host reads and
 // clears the word with qfn_device_status).
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every wait of these kernels gives up after kWaitNs of %globaltimer time
+// (a working kernel waits microseconds), sets a status bit and lets the
+// kernel finish, so that a lost arrival ends in an error status instead of
+// holding the GPU.  (A bound on the iteration count alone is no bound in
+// time: one mbarrier.try_wait may suspend the thread for a while.)
+constexpr unsigned long long kWaitNs = 100ull * 1000 * 1000;   // 100 ms
 constexpr uint32_t kStatusTimeout = 1u;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Deadline check for spin loops: true once kWaitNs have passed since t0
+// (read every 16th iteration).
+__device__ __forceinline__ bool wait_expired(uint32_t i, unsigned long long t0) {
+  return (i & 15u) == 0 && global_ns() - t0 > kWaitNs;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -169,9 +186,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity; false if it timed out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if (wait_expired(i, t0)) return false;
+  }
 }
 
 // Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing

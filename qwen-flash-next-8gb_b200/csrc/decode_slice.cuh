@@ -69,6 +69,13 @@ constexpr int kLSmTotal = kLSmMisc + 1024 + 128;       // + alignment slack for 
 // Per-call-site counters of the zeroing protocol (zero at module load).
 __device__ unsigned long long g_slice_ctr[kLSlots];
 
+// The call-site slot of the next decode call on a device (round robin over
+// kLSlots, shared by the slice and row paths, which share the counters).
+inline int next_decode_slot(int device) {
+  static std::atomic<unsigned int> next_slot[64];
+  return static_cast<int>(next_slot[device].fetch_add(1u) % kLSlots);
+}
+
 struct SliceSplit {
   int grid, K;
   __host__ __device__ int expert_of(int c) const { return static_cast<int>(static_cast<long long>(c) * K / grid); }
@@ -176,6 +183,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
       __threadfence();
       ticket = atomicAdd(&g_slice_ctr[slot], 1ull);
     }
+    __syncwarp();
   }
 
   // B fragments of x for this warp's K-slice [128 warp, +128): lane (g, t), g < 2,
@@ -257,10 +265,14 @@ __global__ void __launch_bounds__(kLThreads, 1)
   auto wait_zeroed = [&]() {
     if (warp == 1 && lane == 0) {
       const unsigned long long target = (ticket / static_cast<unsigned long long>(G) + 1ull) * G;
-      for (uint32_t i = 0; seen < target && i < kSpinLimit; ++i) seen = ld_relaxed_u64(&g_slice_ctr[slot]);
+      const unsigned long long t0 = global_ns();
+      for (uint32_t i = 1; seen < target && !wait_expired(i, t0); ++i) seen = ld_relaxed_u64(&g_slice_ctr[slot]);
       if (seen < target) note_timeout();
       __threadfence();
     }
+    // lanes 1-31 must not reach the caller's block barrier before lane 0:
+    // a barrier reached by a diverged warp completes without its lagging lanes
+    if (warp == 1) __syncwarp();
   };
   if (nbl == 0) {  // no features, or an expert out of range: that one poisons out (NaN), as the other paths do
     if (nf == 0) return;  // (its zeroing is counted)
@@ -279,7 +291,10 @@ __global__ void __launch_bounds__(kLThreads, 1)
     pg[2 * b] = pg[2 * b + 1] = pu[2 * b] = pu[2 * b + 1] = 0.f;
     if (b < nbl) {
       if (!mbar_wait(&bar[b], 0)) note_timeout();
-      if (warp == 0 && b == 0 && nb > 1 && lane == 0) issue_wave_b();
+      if (warp == 0 && b == 0 && nb > 1) {
+        if (lane == 0) issue_wave_b();
+        __syncwarp();
+      }
       // re-read the zeroing counter once block 0 is in (the read at entry may
       // precede the last CTA's count; under the layer's stream a load takes
       // microseconds, so it is issued long before its use)
@@ -440,8 +455,7 @@ inline int launch_moe_decode_slice(const uint8_t* table, int64_t n_blocks, const
     if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "slice decode smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev->device][ti] = true;
   }
-  static std::atomic<unsigned int> next_slot[64];
-  const int slot = static_cast<int>(next_slot[dev->device].fetch_add(1u) % kLSlots);
+  const int slot = next_decode_slot(dev->device);
   // Cooperative (every CTA resident: a CTA waits for the others' zeroing) and a
   // programmatic dependent of the previous kernel in the stream.
   cudaLaunchAttribute attr[2];

@@ -750,6 +750,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       hv.done(h);
     }
   }
+  __syncwarp();   // the role loops end with diverged lanes (elected issuers): reconverge before the block barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, 512);

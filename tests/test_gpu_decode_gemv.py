@@ -142,7 +142,7 @@ def test_moe_decode_repeated_calls_identical(table24, variant):
             synthetic.make_x(2560, 11))
     a, _ = run_decode(table, *args, variant=variant)
     b, _ = run_decode(table, *args, variant=variant)
-    if variant == qmoe.VARIANT_SLICE:
+    if variant in SMALL_K_VARIANTS:
         assert rel_err(a, b) <= REPEAT_GRADE and np.argmax(a) == np.argmax(b)
     else:
         assert np.array_equal(a, b)      # fixed reduction order: bit-reproducible
