@@ -291,10 +291,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
     pg[2 * b] = pg[2 * b + 1] = pu[2 * b] = pu[2 * b + 1] = 0.f;
     if (b < nbl) {
       if (!mbar_wait(&bar[b], 0)) note_timeout();
-      if (warp == 0 && b == 0 && nb > 1) {
-        if (lane == 0) issue_wave_b();
-        __syncwarp();
-      }
+      if (warp == 0 && b == 0 && nb > 1 && lane == 0) issue_wave_b();
       // re-read the zeroing counter once block 0 is in (the read at entry may
       // precede the last CTA's count; under the layer's stream a load takes
       // microseconds, so it is issued long before its use)
@@ -391,7 +388,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
   if (!mbar_wait(&bar[3], 0)) note_timeout();
   if (!mbar_wait(&bar[4], 0)) note_timeout();
   const int kq = lane >> 2;  // lanes 0, 4, 8, 12: which 4 rows of a tile they add into out
-#pragma unroll 2
+#pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int T = warp + kLWarps * i;
     const int r0 = 16 * T + g, r1 = r0 + 8;

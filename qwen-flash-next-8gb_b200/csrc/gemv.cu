@@ -137,18 +137,19 @@ constexpr int kGsMaxTilesPerCta = 16;
 constexpr int kGsSmemBudget = QFN_GEMV_SMEM_KB * 1024;
 
 struct GsLayout {
-  int slots, ring, xs, xraw, red, bar, total;
+  int slots, ring, xs, xraw, red, bar, sc, total;
 };
 
 // Shared memory of the stream path for K and up to `tiles` tiles per CTA:
 // the ring of 16 x K weight slots, x hi/lo (f16), x as loaded (bf16; dead
-// after staging, so it shares its bytes with the per-tile partial sums).
+// after staging, so it shares its bytes with the per-tile partial sums), the
+// CTA's row scales.
 __host__ __device__ inline GsLayout gs_layout(int K, int tiles) {
   GsLayout L;
   const int tile = 16 * K;
   const int red = tiles * kGsWarps * 16 * 4;
   const int scratch = red > 2 * K ? red : 2 * K;
-  const int fixed = 4 * K + scratch + 256 + 128;
+  const int fixed = 4 * K + scratch + 256 + 64 * tiles + 128;
   int slots = (kGsSmemBudget - fixed) / tile;
   slots = slots < 1 ? 1 : (slots > 8 ? 8 : (slots > tiles ? tiles : slots));
   L.slots = slots;
@@ -157,7 +158,8 @@ __host__ __device__ inline GsLayout gs_layout(int K, int tiles) {
   L.xraw = L.xs + 4 * K;      // x as loaded (bf16)
   L.red = L.xraw;             // [tile][warp][16] fp32 partials (after x is staged)
   L.bar = L.xraw + scratch;
-  L.total = L.bar + 256 + 128;  // barriers + alignment slack
+  L.sc = L.bar + 256;           // [16 x tiles] fp32 row scales
+  L.total = L.sc + 64 * tiles + 128;  // + alignment slack
   return L;
 }
 
@@ -200,12 +202,19 @@ __global__ void __launch_bounds__(kGsThreads, 1)
   // next call's CTAs become resident only as this call's leave.
   pdl_wait();
   pdl_launch_dependents();
-  // x first (ordinary loads would queue behind the weight stream), then the tiles.
+  // x and the CTA's row scales first (ordinary loads would queue behind the
+  // weight stream; the scales would otherwise be read at the very end), then
+  // the tiles, one per lane of warp 0 (a single thread issuing bulk copies
+  // back to back takes ~0.2 us per copy).
+  const int64_t nrows = N - 16 * t0 < 16 * nt ? N - 16 * t0 : 16 * nt;
+  const bool sbulk = (reinterpret_cast<uintptr_t>(s) & 15u) == 0 && nrows % 4 == 0;
+  float* sc = reinterpret_cast<float*>(sm + L.sc);
   if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&full[8], 2 * K);
+    mbar_arrive_expect_tx(&full[8], 2 * K + (sbulk ? static_cast<uint32_t>(4 * nrows) : 0u));
     bulk_g2s(sm + L.xraw, x, 2 * K, &full[8]);
-    for (int i = 0; i < nt && i < S; ++i) issue(i);
+    if (sbulk) bulk_g2s(sc, s + 16 * t0, static_cast<uint32_t>(4 * nrows), &full[8]);
   }
+  if (warp == 0 && lane < S && lane < nt) issue(lane);
 
   // x -> f16 hi/lo * 2^ex (thread u owns k = u, u + 512, ...)
   if (!mbar_wait(&full[8], 0)) atomicOr(&g_gemv_status, kStatusTimeout);
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(kGsThreads, 1)
     if (row >= N) continue;
     float acc = 0.f;
     for (int w = 0; w < kGsWarps; ++w) acc += red[(i * kGsWarps + w) * 16 + rr];
-    const float v = ldexpf(acc, -ex) * s[row];
+    const float v = ldexpf(acc, -ex) * (sbulk ? sc[r] : s[row]);
     if (kOutF32) static_cast<float*>(y)[row] = v;
     else static_cast<__nv_bfloat16*>(y)[row] = __float2bfloat16_rn(v);
   }
