@@ -50,7 +50,7 @@ def router_case(T, E, seed, dup_rows=0):
 
 
 @pytest.mark.parametrize("T,E,topk,seed", [(1, 512, 10, 1), (7, 512, 10, 2), (64, 512, 10, 3), (3, 128, 4, 4),
-                                           (2, 1024, 32, 5)])
+                                           (2, 1024, 32, 5), (1, 128, 4, 6), (1, 1024, 32, 7), (1, 4, 4, 8)])
 def test_route_fused_matches_oracle(T, E, topk, seed):
     x, w = router_case(T, E, seed)
     s2_table = torch.from_numpy(synthetic.make_s2(3 * E, seed=seed, spread=True).reshape(3, E, 3)).to(DEV)
@@ -77,8 +77,9 @@ def test_route_fused_matches_oracle(T, E, topk, seed):
     assert torch.equal(r["s2"], s2_table[layer][r["ti"].long()])
 
 
-def test_route_fused_ties_go_to_the_lower_expert():
-    x, w = router_case(5, 512, 11, dup_rows=256)         # experts e and e + 256 have equal logits
+@pytest.mark.parametrize("T", [1, 5])
+def test_route_fused_ties_go_to_the_lower_expert(T):
+    x, w = router_case(T, 512, 11, dup_rows=256)         # experts e and e + 256 have equal logits
     r = routing.route_fused(x, w, 10)
     logits = r["logits"].float().cpu().numpy()
     ti_ref, coef_ref = oracle.route(logits, 10)
