@@ -417,23 +417,25 @@ def prefill_record(ctx):
     parity = ctx.parity([e], ok, n)
     del out0
 
-    # e2e: host buffers in (x, ti, tv) and the fp32 result out, every step
+    # e2e: host buffers in (x, ti, tv) and the fp32 result out, every step,
+    # pipelined as a serving loop runs it: step i + 1's inputs copy in on one
+    # copy stream and step i - 1's result copies out on another while step i
+    # computes (two device buffer sets); the timed region holds E whole steps,
+    # the first step's copy in and the last step's copy out included.
     h_x = [x.cpu().pin_memory() for x in xs]
     h_ti = [t.cpu().pin_memory() for t in tis]
     h_tv = [t.cpu().pin_memory() for t in tvs]
-    h_out = torch.empty(T, HID, dtype=torch.float32).pin_memory()
-    d_x, d_ti, d_tv = torch.empty_like(xs[0]), torch.empty_like(tis[0]), torch.empty_like(tvs[0])
-    h2d = d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2
+    h_out = [torch.empty(T, HID, dtype=torch.float32).pin_memory() for _ in range(2)]
+    d_in = [(torch.empty_like(xs[0]), torch.empty_like(tis[0]), torch.empty_like(tvs[0])) for _ in range(2)]
+    h2d = d_in[0][0].numel() * 2 + d_in[0][1].numel() * 8 + d_in[0][2].numel() * 2
     d2h = T * HID * 4
-
-    def e2e_step(i):
-        d_x.copy_(h_x[i % R], non_blocking=True)
-        d_ti.copy_(h_ti[i % R], non_blocking=True)
-        d_tv.copy_(h_tv[i % R], non_blocking=True)
-        h_out.copy_(call(d_x, d_ti, d_tv), non_blocking=True)
-
     E = min(args.e2e_steps, args.steps)
-    ms_e2e = ctx.timed(e2e_step, E, 2)
+    e2e_pipelined = make_e2e_pipeline(
+        lambda i, k: (d_in[k][0].copy_(h_x[i % R], non_blocking=True), d_in[k][1].copy_(h_ti[i % R], non_blocking=True),
+                      d_in[k][2].copy_(h_tv[i % R], non_blocking=True)),
+        lambda i, k: call(*d_in[k]),
+        lambda i, k, out: h_out[k].copy_(out, non_blocking=True))
+    ms_e2e = ctx.timed(lambda i: e2e_pipelined(E), 1, 2) / E
 
     breakdown = ep_breakdown(ctx, shard, table, s2, xs[0], tis[0], tvs[0]) if shard is not None and \
         args.ep_mode == "ag" else None
@@ -453,7 +455,8 @@ def prefill_record(ctx):
         "e2e": {"value": world * T / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": E, "ms_per_step": ms_e2e,
                 "path": ("qmoe.moe_prefill" if world == 1 else f"ep.{ep_fn.__name__}") +
-                        " (public API) with pinned host x, ti, tv in and the fp32 result out"},
+                        " (public API) with pinned host x, ti, tv in and the fp32 result out, pipelined over two "
+                        "buffer sets (copies in and out on two copy streams overlap the neighbouring steps' compute)"},
         "roofline": {"bound": "hbm", "achieved": gbs_rank, "peak": hbm, "unit": "GB/s", "frac": gbs_rank / hbm,
                      "peak_kind": kind, "tensor_tflops": tflops_rank, "tensor_peak": tc,
                      "tensor_frac": tflops_rank / tc,
@@ -509,6 +512,48 @@ def ep_breakdown(ctx, shard, table, s2, x, ti, tv, reps=10):
         b = ctx.args.ep_sm_budget
         _lib.set_prefill_sm_budget(b if b > 0 else sms + b)
     return res
+
+
+def make_e2e_pipeline(copy_in, compute, copy_out):
+    """A serving loop over n steps with two device buffer sets: copy_in(i, k)
+    (host -> set k) on a copy stream, compute(i, k) -> device result on the
+    current stream, copy_out(i, k, result) (-> host buffer k) on a second copy
+    stream; step i + 1's copy in and step i - 1's copy out overlap step i's
+    compute.  The returned run(n) leaves the current stream waiting for the
+    last copy out."""
+    import torch
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    outs = [None, None]
+
+    def run(n):
+        cur = torch.cuda.current_stream()   # (inside a graph capture: the capturing stream)
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            copy_in(0, 0)
+            ready[0].record(s_in)
+        for i in range(n):
+            k = i & 1
+            if i + 1 < n:                       # the next step's inputs, once step i - 1 has read set 1 - k
+                with torch.cuda.stream(s_in):
+                    if i >= 1:
+                        s_in.wait_event(done[1 - k])
+                    copy_in(i + 1, 1 - k)
+                    ready[1 - k].record(s_in)
+            cur.wait_event(ready[k])
+            if i >= 2:                          # result buffer k is free once step i - 2's copy out is done
+                cur.wait_event(copied[k])
+            outs[k] = compute(i, k)
+            done[k].record(cur)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[k])
+                copy_out(i, k, outs[k])
+                copied[k].record(s_out)
+        cur.wait_stream(s_out)
+    return run
 
 
 def ctx_all_gather(ctx, t):
@@ -609,26 +654,36 @@ def decode_record(ctx, steps):
         ok = ok and int(y.argmax()) == int(ref.argmax())
     parity = ctx.parity(errs, ok, 2)
 
-    # e2e: public API, eager, host inputs copied in and outputs copied out every step
+    # e2e: public API, host inputs copied in and outputs copied out every step
     E = min(args.e2e_steps, R)
     h_x = x[:E].cpu().pin_memory()
     h_sidx, h_s2, h_coef = sidx[:E].cpu().pin_memory(), s2[:E].cpu().pin_memory(), coef[:E].cpu().pin_memory()
-    d_x, d_sidx, d_s2, d_coef = torch.empty_like(x[0]), torch.empty_like(sidx[0]), torch.empty_like(s2[0]), \
-        torch.empty_like(coef[0])
+    d_in = [(torch.empty_like(x[0]), torch.empty_like(sidx[0]), torch.empty_like(s2[0]), torch.empty_like(coef[0]))
+            for _ in range(2)]
     h_out = torch.empty(E, L, HID).pin_memory()
-    h2d = d_x.numel() * 2 + d_sidx.numel() * 4 + d_s2.numel() * 4 + d_coef.numel() * 4
-    per_layer = [(d_sidx[l], d_s2[l], d_coef[l], d_x[l]) for l in range(L)]
+    h2d = d_in[0][0].numel() * 2 + d_in[0][1].numel() * 4 + d_in[0][2].numel() * 4 + d_in[0][3].numel() * 4
 
-    def e2e_step(i):
-        r = i % E
-        d_x.copy_(h_x[r], non_blocking=True)
-        d_sidx.copy_(h_sidx[r], non_blocking=True)
-        d_s2.copy_(h_s2[r], non_blocking=True)
-        d_coef.copy_(h_coef[r], non_blocking=True)
-        outs = [qmoe.moe_decode(table.slots, si, s2l, cl, xl, hb, ob) for si, s2l, cl, xl in per_layer]
-        h_out[r].copy_(torch.stack(outs), non_blocking=True)
+    def e2e_in(i, k):
+        for d, h in zip(d_in[k], (h_x, h_sidx, h_s2, h_coef)):
+            d.copy_(h[i % E], non_blocking=True)
 
-    ms_e2e = ctx.timed(e2e_step, E, 3)
+    def e2e_compute(i, k):
+        dx, ds, d2, dc = d_in[k]
+        return torch.stack([qmoe.moe_decode(table.slots, ds[l], d2[l], dc[l], dx[l], hb, ob) for l in range(L)])
+
+    # the steps as a serving loop runs them: each step's copies in, its 48 calls
+    # and its copy out, pipelined over two buffer sets (the next step's inputs and
+    # the previous step's outputs copy during this step's layers), E steps in one
+    # CUDA graph (host launch cost off the critical path)
+    e2e_pipelined = make_e2e_pipeline(e2e_in, e2e_compute,
+                                      lambda i, k, out: h_out[i % E].copy_(out, non_blocking=True))
+    e2e_pipelined(2)
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_pipelined(E)
+    ms_e2e = ctx.timed(lambda i: e2e_graph.replay(), 4, 2) / E
+    del e2e_graph
     hbm, _, kind = peaks()
     achieved = LAYER_BYTES / (us_layer * 1e-6) / 1e9
     rec = {
@@ -641,7 +696,10 @@ def decode_record(ctx, steps):
                    "routes": R, "layer_bytes": LAYER_BYTES,
                    "l2": "no flush: each step streams 1.33 GB of distinct expert bytes (> 126 MB L2)"},
         "e2e": {"value": E * step_bytes / (ms_e2e * E * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": L * HID * 4, "ms_per_step": ms_e2e, "path": "qmoe.moe_decode per layer (eager)"},
+                "d2h_bytes_per_step": L * HID * 4, "ms_per_step": ms_e2e,
+                "path": "qmoe.moe_decode per layer (public API) with pinned host x, sidx, s2, coef in and the 48 "
+                        "fp32 outputs out every step, steps pipelined over two buffer sets (copies on two copy "
+                        f"streams), {E} steps per CUDA graph"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "frac_of_8tbs": achieved / 8000.0,
                      "traffic": TRAFFIC["decode"] if args.variant in (0, 4) else None, "per_launch_bytes": LAYER_BYTES,
@@ -726,14 +784,23 @@ def gemv_record(ctx, steps):
     # e2e: the public API per call, x copied in from pinned host memory, y copied back
     qs, ss, xs = per_shape[GEMV_SHAPES[0]]
     h_x = [x.cpu().pin_memory() for x in xs]
-    h_y = torch.empty(N0, dtype=torch.bfloat16).pin_memory()
-    d_x = torch.empty_like(xs[0])
+    h_y = [torch.empty(N0, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    d_x = [torch.empty_like(xs[0]) for _ in range(2)]
+    e2e_pipelined = make_e2e_pipeline(
+        lambda i, k: d_x[k].copy_(h_x[i % 4], non_blocking=True),
+        lambda i, k: fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], d_x[k]),
+        lambda i, k, y: h_y[k].copy_(y, non_blocking=True))
 
-    def e2e_call(i):
-        d_x.copy_(h_x[i % 4], non_blocking=True)
-        h_y.copy_(fp8gemv.gemv(qs[i % GEMV_COPIES], ss[i % GEMV_COPIES], d_x), non_blocking=True)
-
-    ms_e2e = ctx.timed(e2e_call, 256, 8)
+    # GEMV_CALLS calls, each with its copy in and copy out (pipelined: call i + 1's x
+    # copies in and call i - 1's y copies out during call i), in one CUDA graph, as an
+    # engine's decode step captures its projections
+    e2e_pipelined(2)
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_pipelined(GEMV_CALLS)
+    ms_e2e = ctx.timed(lambda i: e2e_graph.replay(), 16, 3) / GEMV_CALLS
+    del e2e_graph
     hbm, _, kind = peaks()
     achieved = b0 / (us_call[GEMV_SHAPES[0]] * 1e-6) / 1e9
     rec = {
@@ -749,7 +816,9 @@ def gemv_record(ctx, steps):
                          f"({GEMV_COPIES * N0 * K0 / 1e6:.0f} MB > 2 x 126 MB L2)"},
         "e2e": {"value": ctx.world * b0 / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": K0 * 2,
                 "d2h_bytes_per_step": N0 * 2, "us_per_call": ms_e2e * 1e3,
-                "path": "fp8gemv.gemv (public API, eager) with x from pinned host memory and y copied back"},
+                "path": "fp8gemv.gemv (public API) with x from pinned host memory and y copied back every call, "
+                        f"{GEMV_CALLS} calls per CUDA graph, copies on two copy streams overlapping the neighbouring "
+                        "calls"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "kernel": "gemv_stream_kernel",
                      # the capture is of the 2560x4096 shape; scaled to this shape by its algorithmic bytes
@@ -856,20 +925,25 @@ def batch_decode_record(ctx, steps):
         ok, n = ok and o, n + k
     parity = ctx.parity(errs, ok, n)
 
-    # e2e: per step every layer's x, ti, tv from pinned host memory and its fp32 output back
+    # e2e: per step every layer's x, ti, tv from pinned host memory and its fp32
+    # output back, pipelined over two buffer sets (the next step's copy in and
+    # the previous step's copy out overlap this step's layers)
     h_x, h_ti, h_tv = xs[0].cpu().pin_memory(), ti[0].cpu().pin_memory(), tv[0].cpu().pin_memory()
-    h_out = torch.empty(L, B, HID, dtype=torch.float32).pin_memory()
-    d_x, d_ti, d_tv = torch.empty_like(xs[0]), torch.empty_like(ti[0]), torch.empty_like(tv[0])
+    h_out = [torch.empty(L, B, HID, dtype=torch.float32).pin_memory() for _ in range(2)]
+    d_in = [(torch.empty_like(xs[0]), torch.empty_like(ti[0]), torch.empty_like(tv[0])) for _ in range(2)]
+    d_x = d_in[0][0]
 
-    def e2e_step(i):
-        d_x.copy_(h_x, non_blocking=True)
-        d_ti.copy_(h_ti, non_blocking=True)
-        d_tv.copy_(h_tv, non_blocking=True)
+    def e2e_out(i, k, outs):
         for l in range(L):
-            h_out[l].copy_(layer(d_x[l], d_ti[l], d_tv[l], l), non_blocking=True)
+            h_out[k][l].copy_(outs[l], non_blocking=True)
 
+    e2e_pipelined = make_e2e_pipeline(
+        lambda i, k: (d_in[k][0].copy_(h_x, non_blocking=True), d_in[k][1].copy_(h_ti, non_blocking=True),
+                      d_in[k][2].copy_(h_tv, non_blocking=True)),
+        lambda i, k: [layer(d_in[k][0][l], d_in[k][1][l], d_in[k][2][l], l) for l in range(L)],
+        e2e_out)
     E = min(args.e2e_steps, 8)
-    ms_e2e = ctx.timed(e2e_step, E, 1)
+    ms_e2e = ctx.timed(lambda i: e2e_pipelined(E), 1, 1) / E
     hbm, _, kind = peaks()
     rec = {
         "metric": BD_METRIC, "value": world * B / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
@@ -882,9 +956,11 @@ def batch_decode_record(ctx, steps):
                    "parallelism": "single GPU" if world == 1 else
                    f"expert-parallel x{world} (NCCL {'all-gather + reduce-scatter' if args.ep_mode == 'ag' else 'all-to-all'}, eager)"},
         "e2e": {"value": world * B / (ms_e2e * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": d_x.numel() * 2 + d_ti.numel() * 8 + d_tv.numel() * 2,
+                "h2d_bytes_per_step": d_in[0][0].numel() * 2 + d_in[0][1].numel() * 8 + d_in[0][2].numel() * 2,
                 "d2h_bytes_per_step": L * B * HID * 4, "ms_per_step": ms_e2e,
-                "path": "qmoe.moe_prefill per layer (public API, eager) with pinned host inputs and outputs"},
+                "path": ("qmoe.moe_prefill" if shard is None else "ep.moe_prefill_ep" + ("_ag" if args.ep_mode == "ag" else "")) +
+                        " per layer (public API, eager) with pinned host inputs and outputs, pipelined over two "
+                        "buffer sets (copies on two copy streams overlap the neighbouring steps' layers)"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                      "peak_kind": kind, "traffic": None,
                      "kernel": "qfn_moe_prefill per layer (7 launches; the time is the whole step's)"},
