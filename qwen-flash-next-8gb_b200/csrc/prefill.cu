@@ -7,7 +7,8 @@
 // with the weights of qmoe.block_deq (qmoe.py:93-111): e2m1 code x E4M3 block
 // scale (one per 16 k) x per-tensor ws2.
 //
-// Pipeline (one stream, eight launches):
+// Pipeline (one stream: a memset of out, then seven launches, each a
+// programmatic dependent of the one before):
 //  1. pf_count / pf_plan / pf_scatter: (token, slot) pairs grouped by expert
 //     (a counting sort over 64 slices of the pairs), and tiles of up to 128
 //     pairs of one expert.
@@ -19,8 +20,7 @@
 //     memory (e2m1 x E4M3 is exact in f16), B = the tile's x rows (TMA,
 //     128-byte swizzle).  Epilogue: h = silu(ws2_g g) * (ws2_u u) in fp32.
 //  4. pf_hpack: h rows -> f16 hi + lo (h * 2^e = hi + lo, one e per pair).
-//  5. out = 0.
-//  6. pf_gemm<DOWN>: per (tile, 128 output rows): A = down rows, B = the
+//  5. pf_gemm<DOWN>: per (tile, 128 output rows): A = down rows, B = the
 //     tile's h hi rows followed by its h lo rows (one MMA computes both;
 //     the epilogue sums the two column blocks: ~22-bit h), and adds
 //     coef * ws2_d * D into out with fp32 atomics (as index_add_ on CUDA).
@@ -33,6 +33,8 @@
 // epilogue of one job overlaps the next job's MMAs).  Every wait is bounded;
 // a wait that runs out sets a status bit.
 #include <cuda_fp16.h>
+
+#include <utility>
 
 #include "common.cuh"
 #include "host.cuh"
@@ -100,11 +102,32 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total)
 // tiles, hdr[1] = number of valid pairs; offs[E + 1]; pair_tok[P], pair_w[P]
 // (grouped by expert: by slice, then in shared-atomic order within a slice);
 // tile_e/tile_p0/tile_n.  Scratch: hist/base [kPfRouteCtas][E].
+// Launches of the prefill pipeline: each a programmatic dependent of the
+// previous kernel in the stream (its launch and prologue overlap that
+// kernel's tail; it waits with griddepcontrol.wait before touching memory).
+template <typename... KArgs, typename... Args>
+static cudaError_t pf_launch(void (*k)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 constexpr int kPfRouteCtas = 64;  // CTAs of the count and scatter passes, each a contiguous slice of the pairs
 
 // (a) per-slice expert counts
 template <typename TI>
 __global__ void __launch_bounds__(1024) pf_count_kernel(const TI* __restrict__ ti, int64_t P, int E, int* hist) {
+  pdl_wait();   // inputs come from the previous kernel in the stream
+  pdl_launch_dependents();
   __shared__ int cnt[kPfMaxExperts];
   const int tid = threadIdx.x;
   for (int i = tid; i < E; i += blockDim.x) cnt[i] = 0;
@@ -122,6 +145,8 @@ __global__ void __launch_bounds__(1024) pf_count_kernel(const TI* __restrict__ t
 // (b) one CTA (thread = expert): offsets, tiles, and each slice's first slot per expert
 __global__ void __launch_bounds__(1024) pf_plan_kernel(const int* __restrict__ hist, int G, int E, int* hdr, int* offs,
                                                        int* tile_e, int* tile_p0, int* tile_n, int* base) {
+  pdl_wait();   // inputs come from the previous kernel in the stream
+  pdl_launch_dependents();
   __shared__ int tmp[32];
   const int tid = threadIdx.x;
   int c = 0;
@@ -156,6 +181,8 @@ template <typename TI, bool kTvBf16>
 __global__ void __launch_bounds__(1024) pf_scatter_kernel(const TI* __restrict__ ti, const void* __restrict__ tv,
                                                           int64_t P, int topk, int E, const int* __restrict__ base,
                                                           int* pair_tok, float* pair_w) {
+  pdl_wait();   // inputs come from the previous kernel in the stream
+  pdl_launch_dependents();
   __shared__ int cur[kPfMaxExperts];
   const int tid = threadIdx.x;
   for (int i = tid; i < E; i += blockDim.x) cur[i] = base[blockIdx.x * E + i];
@@ -177,12 +204,16 @@ template <typename TI>
 static int pf_route(const TI* ti, const void* tv, bool tv_bf16, int64_t P, int topk, int E, int* hist, int* base,
                     int* hdr, int* offs, int* tile_e, int* tile_p0, int* tile_n, int* pair_tok, float* pair_w,
                     cudaStream_t st) {
-  pf_count_kernel<TI><<<kPfRouteCtas, 1024, 0, st>>>(ti, P, E, hist);
-  pf_plan_kernel<<<1, 1024, 0, st>>>(hist, kPfRouteCtas, E, hdr, offs, tile_e, tile_p0, tile_n, base);
-  if (tv_bf16)
-    pf_scatter_kernel<TI, true><<<kPfRouteCtas, 1024, 0, st>>>(ti, tv, P, topk, E, base, pair_tok, pair_w);
-  else
-    pf_scatter_kernel<TI, false><<<kPfRouteCtas, 1024, 0, st>>>(ti, tv, P, topk, E, base, pair_tok, pair_w);
+  cudaError_t e = pf_launch(pf_count_kernel<TI>, kPfRouteCtas, 1024, 0, st, ti, P, E, hist);
+  if (e == cudaSuccess)
+    e = pf_launch(pf_plan_kernel, 1, 1024, 0, st, static_cast<const int*>(hist), kPfRouteCtas, E, hdr, offs, tile_e,
+                  tile_p0, tile_n, base);
+  if (e == cudaSuccess)
+    e = tv_bf16 ? pf_launch(pf_scatter_kernel<TI, true>, kPfRouteCtas, 1024, 0, st, ti, tv, P, topk, E,
+                            static_cast<const int*>(base), pair_tok, pair_w)
+                : pf_launch(pf_scatter_kernel<TI, false>, kPfRouteCtas, 1024, 0, st, ti, tv, P, topk, E,
+                            static_cast<const int*>(base), pair_tok, pair_w);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "pf_route launch: %s", cudaGetErrorString(e));
   return check_launch("pf_route");
 }
 
@@ -209,6 +240,8 @@ __global__ void __launch_bounds__(32 * kPfRowWarps) pf_gather_x_kernel(const uin
                                                                       const int* __restrict__ hdr,
                                                                       const int* __restrict__ pair_tok,
                                                                       __half* x16, int* pair_ex) {
+  pdl_wait();   // inputs come from the previous kernel in the stream
+  pdl_launch_dependents();
   constexpr int kChunks = kHid / 8 / 32;  // 16-byte chunks per lane: 10
   const int lane = threadIdx.x & 31;
   const int p = blockIdx.x * kPfRowWarps + (threadIdx.x >> 5);
@@ -248,6 +281,8 @@ __global__ void __launch_bounds__(32 * kPfRowWarps) pf_gather_x_kernel(const uin
 __global__ void __launch_bounds__(32 * kPfRowWarps) pf_hpack_kernel(const float* __restrict__ h32,
                                                                    const int* __restrict__ hdr, __half* hhi,
                                                                    __half* hlo, int* pair_eh) {
+  pdl_wait();   // inputs come from the previous kernel in the stream
+  pdl_launch_dependents();
   constexpr int kChunks = kInter / 4 / 32;  // float4 per lane: 5
   const int lane = threadIdx.x & 31;
   const int p = blockIdx.x * kPfRowWarps + (threadIdx.x >> 5);
@@ -454,6 +489,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // (the prologue above overlaps the previous kernel's tail; the tile lists,
+  // activations and out come from earlier kernels in the stream)
+  pdl_wait();
+  pdl_launch_dependents();
   const int n_jobs = args.hdr[0] * C::kSub;
 
   if (warp == 0) {
@@ -799,7 +838,8 @@ static int pf_launch_gemm(const PfMaps& maps, const PfArgs& a, const DeviceInfo*
     attr_set[dev->device] = true;
   }
   const int grid = dev->pf_ctas > 0 && dev->pf_ctas < dev->sm_count ? dev->pf_ctas : dev->sm_count;
-  pf_gemm_kernel<MODE><<<grid, kPfThreads, smem, st>>>(maps, a);
+  cudaError_t e = pf_launch(pf_gemm_kernel<MODE>, grid, kPfThreads, smem, st, maps, a);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "pf_gemm launch: %s", cudaGetErrorString(e));
   return check_launch(MODE == kGateUp ? "pf_gemm<gate/up>" : "pf_gemm<down>");
 }
 
@@ -853,6 +893,12 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   __half* hlo = reinterpret_cast<__half*>(ws + W.hlo);
   const int64_t P = T * topk;
 
+  // 0. out = 0 (the down GEMM adds into it; zeroed first so that the kernels
+  // after it follow one another as programmatic dependents)
+  {
+    cudaError_t e0 = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * kHid * sizeof(float), st);
+    if (e0 != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_moe_prefill: memset: %s", cudaGetErrorString(e0));
+  }
   // 1. routing
   int* rhist = reinterpret_cast<int*>(ws + W.rhist);
   int* rbase = reinterpret_cast<int*>(ws + W.rbase);
@@ -863,8 +909,9 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   if (rc) return rc;
   // 2. x rows in pair order
   const unsigned row_ctas = static_cast<unsigned>((P + kPfRowWarps - 1) / kPfRowWarps);
-  pf_gather_x_kernel<<<row_ctas, 32 * kPfRowWarps, 0, st>>>(static_cast<const uint16_t*>(x), hdr, pair_tok, x16,
-                                                            pair_ex);
+  cudaError_t e = pf_launch(pf_gather_x_kernel, row_ctas, 32 * kPfRowWarps, 0, st, static_cast<const uint16_t*>(x),
+                            static_cast<const int*>(hdr), static_cast<const int*>(pair_tok), x16, pair_ex);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "pf_gather_x launch: %s", cudaGetErrorString(e));
   if ((rc = check_launch("pf_gather_x"))) return rc;
 
   // tensor maps
@@ -914,11 +961,11 @@ extern "C" int qfn_moe_prefill(const void* x, int64_t T, const void* ti, int ti_
   PfArgs a{hdr, tile_e, tile_p0, tile_n, pair_tok, pair_w, pair_ex, table, base, s2l, h32, out};
   if ((rc = pf_launch_gemm<kGateUp>(gu_maps, a, dev, st))) return rc;
   // 4. h -> f16 hi/lo
-  pf_hpack_kernel<<<row_ctas, 32 * kPfRowWarps, 0, st>>>(h32, hdr, hhi, hlo, pair_eh);
+  e = pf_launch(pf_hpack_kernel, row_ctas, 32 * kPfRowWarps, 0, st, static_cast<const float*>(h32),
+                static_cast<const int*>(hdr), hhi, hlo, pair_eh);
+  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "pf_hpack launch: %s", cudaGetErrorString(e));
   if ((rc = check_launch("pf_hpack"))) return rc;
-  // 5. out = 0, 6. down + combine
-  cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(T) * kHid * sizeof(float), st);
-  if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_moe_prefill: memset: %s", cudaGetErrorString(e));
+  // 5. down + combine (into out, zeroed at entry)
   a.pair_ex = pair_eh;
   return pf_launch_gemm<kDown>(dn_maps, a, dev, st);
 }
