@@ -316,6 +316,42 @@ int qfn_set_prefill_sm_budget(int n_sms);
  */
 int qfn_prefill_status(unsigned int* status, int clear);
 
+/*
+ * qfn_moe_prefill_ep -- the expert-parallel MoE layer (batched prefill or
+ * batched decode) over an NCCL communicator, for callers that run NCCL
+ * themselves (the torch path is ep.moe_prefill_ep_ag; the reference is
+ * single-GPU).  Every rank passes its own T tokens and the same T:
+ *   all-gather x and the routing over `comm`, map the ids through
+ *   `local_of`, the grouped GEMM of qfn_moe_prefill over all W x T tokens and
+ *   this rank's n_local experts, reduce-scatter (sum) of the fp32 partial
+ *   sums: out = this rank's tokens' MoE output (as qfn_moe_prefill over all
+ *   512 experts would give, up to the order of the fp32 sums).
+ *   x: bf16[T][2560] device; ti, tv, topk as qfn_moe_prefill (ids are global
+ *   expert ids in [0, n_experts)); table/n_blocks/base/s2l: this rank's
+ *   expert table (local expert i = block base + i, ws2 s2l[i]); local_of:
+ *   int32[n_experts] device, the local index of each global expert on this
+ *   rank or -1; comm: an ncclComm_t of W ranks whose device is the current
+ *   one; out: f32[T][2560]; workspace: qfn_moe_prefill_ep_workspace(T, topk,
+ *   n_local, W) bytes, 256-byte aligned.  All work, collectives included, is
+ *   queued on `stream`; libnccl.so.2 is resolved at run time.
+ */
+size_t qfn_moe_prefill_ep_workspace(int64_t T, int topk, int n_local, int world);
+int qfn_moe_prefill_ep(const void* x, int64_t T, const void* ti, int ti_is_int64,
+                       const void* tv, int tv_dtype, int topk, const uint8_t* table,
+                       int64_t n_blocks, int64_t base, const float* s2l, int n_local,
+                       const int32_t* local_of, int n_experts, void* comm, float* out,
+                       void* workspace, size_t workspace_bytes, qfn_stream_t stream);
+
+/*
+ * NCCL bootstrap for callers without one: qfn_nccl_unique_id writes the
+ * 128-byte ncclUniqueId (one rank creates it and sends it to the others by
+ * any means); qfn_nccl_comm_init makes this rank's communicator on the
+ * current device; qfn_nccl_comm_destroy releases it.
+ */
+int qfn_nccl_unique_id(void* id_out);
+int qfn_nccl_comm_init(void** comm_out, int world, int rank, const void* id);
+int qfn_nccl_comm_destroy(void* comm);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,12 +36,17 @@ SIGNATURES = {
     "qfn_set_prefill_sm_budget": [_I],
     "qfn_moe_route": [_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "qfn_shared_expert": [_P, _I64, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P],
+    "qfn_moe_prefill_ep_workspace": [_I64, _I, _I, _I],
+    "qfn_moe_prefill_ep": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, ctypes.c_size_t, _P],
+    "qfn_nccl_unique_id": [_P],
+    "qfn_nccl_comm_init": [_P, _I, _I, _P],
+    "qfn_nccl_comm_destroy": [_P],
     "qfn_shared_expert_gate_up": [_P, _I64, _P, _P, _P, _I, _P, _P, _P],
     "qfn_shared_expert_down": [_P, _I, _I64, _P, _P, _P, _P, _P],
     "qfn_deltanet_step": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
 }
 # entry points whose return value is not an int status
-RESTYPES = {"qfn_moe_prefill_workspace": ctypes.c_size_t}
+RESTYPES = {"qfn_moe_prefill_workspace": ctypes.c_size_t, "qfn_moe_prefill_ep_workspace": ctypes.c_size_t}
 
 
 class QfnError(RuntimeError):

@@ -45,7 +45,7 @@ def build(force=False, verbose=False):
     if not force and not needs_build():
         return LIB
     tmp = LIB + ".tmp"
-    cmd = [NVCC, *ARCH, *FLAGS, *sources(), "-o", tmp, "-lcuda"]
+    cmd = [NVCC, *ARCH, *FLAGS, *sources(), "-o", tmp, "-lcuda", "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))

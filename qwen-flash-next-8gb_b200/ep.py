@@ -30,11 +30,14 @@ sizes and no host synchronisation: a layer of it can be captured in a CUDA
 graph.  It moves every token to every rank, so it suits small batches
 (batched decode); the all-to-all exchange moves only routed rows.
 """
+import ctypes
+
 import numpy as np
 import torch
 import torch.distributed as dist
 
 import qmoe
+from _lib import DTYPE_BF16, DTYPE_F32, check, lib, on_device, require_cuda, stream_of
 
 
 class ExpertShard:
@@ -210,4 +213,55 @@ def moe_prefill_ep_ag(x, ti, tv, table, s2, L, shard, group=None, compute=None, 
             scatters.append((dist.reduce_scatter_tensor(out[a:b], y_all, group=group, async_op=True), y_all))
     for w, _ in scatters:
         w.wait()
+    return out
+
+
+class NcclComm:
+    """An NCCL communicator made through libqfn's bootstrap (qfn_nccl_comm_init)
+    on the current device, for the C-ABI expert-parallel layer
+    (moe_prefill_ep_nccl).  Rank 0 makes the 128-byte id with unique_id() and
+    every rank receives it by its own means."""
+
+    @staticmethod
+    def unique_id():
+        buf = ctypes.create_string_buffer(128)
+        check(lib().qfn_nccl_unique_id(buf), "qfn_nccl_unique_id")
+        return buf.raw
+
+    def __init__(self, world, rank, uid):
+        if len(uid) != 128:
+            raise ValueError("the NCCL unique id is 128 bytes")
+        self.world, self.rank = world, rank
+        self.ptr = ctypes.c_void_p()
+        check(lib().qfn_nccl_comm_init(ctypes.byref(self.ptr), world, rank, ctypes.create_string_buffer(uid, 128)),
+              "qfn_nccl_comm_init")
+
+    def close(self):
+        if self.ptr:
+            check(lib().qfn_nccl_comm_destroy(self.ptr), "qfn_nccl_comm_destroy")
+            self.ptr = ctypes.c_void_p()
+
+
+def moe_prefill_ep_nccl(x, ti, tv, table, s2, L, shard, comm):
+    """moe_prefill_ep_ag through the C ABI (qfn_moe_prefill_ep): the exchange
+    and the grouped GEMM in one library call over an NCCL communicator
+    (`comm`: an NcclComm or a raw ncclComm_t pointer), for engines that drive
+    NCCL without torch.distributed.  Arguments as moe_prefill_ep."""
+    for name, t in (("x", x), ("ti", ti), ("tv", tv), ("table", table), ("s2", s2)):
+        require_cuda(name, t)
+    T, K = ti.shape
+    dev = x.device
+    mine = shard.maps(dev)[2]
+    E_r = s2.shape[0]
+    out = torch.empty(T, x.shape[1], dtype=torch.float32, device=dev)
+    L_ = lib()
+    nbytes = L_.qfn_moe_prefill_ep_workspace(T, K, E_r, shard.world)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    ptr = comm.ptr if isinstance(comm, NcclComm) else comm
+    with on_device(dev):
+        rc = L_.qfn_moe_prefill_ep(x.data_ptr(), T, ti.data_ptr(), int(ti.dtype == torch.int64), tv.data_ptr(),
+                                   DTYPE_BF16 if tv.dtype == torch.bfloat16 else DTYPE_F32, K, table.data_ptr(),
+                                   table.shape[0], int(L) * E_r, s2.data_ptr(), E_r, mine.data_ptr(), len(mine), ptr,
+                                   out.data_ptr(), ws.data_ptr(), nbytes, stream_of(out))
+    check(rc, "qfn_moe_prefill_ep")
     return out

@@ -113,6 +113,16 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert dn(4, 2, 96, 128) == 4
     assert dn(4, 2, 128, 100) == 4
     assert lib.qfn_set_prefill_sm_budget(-1) == 1
+    # expert-parallel layer over NCCL: nulls (the communicator first), sizes, workspace query
+    ep = lambda comm, T, nl: lib.qfn_moe_prefill_ep(fake, T, fake, 1, fake, 0, 10, fake, 8, 0, fake, nl, fake, 16,
+                                                    comm, fake, fake, 1 << 20, None)
+    assert ep(None, 4, 2) == 1
+    assert ep(fake, 0, 2) == 1
+    assert ep(fake, 4, 0) == 1
+    assert lib.qfn_moe_prefill_ep_workspace(0, 10, 2, 2) == 0
+    assert lib.qfn_moe_prefill_ep_workspace(64, 10, 2, 2) > lib.qfn_moe_prefill_workspace(128, 10, 2)
+    assert lib.qfn_nccl_comm_init(None, 2, 0, fake) == 1
+    assert lib.qfn_nccl_comm_destroy(None) == 1
 
 
 def test_python_wrappers_reject_cpu_tensors():

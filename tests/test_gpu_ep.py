@@ -47,6 +47,12 @@ def _worker(rank, port, results, mode="a2a"):
         own = shard.experts
         toks = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
         fn = ep.moe_prefill_ep if mode == "a2a" else ep.moe_prefill_ep_ag
+        comm = None
+        if mode == "nccl_c":   # the C-ABI layer over libqfn's own NCCL communicator
+            uid = [ep.NcclComm.unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            comm = ep.NcclComm(WORLD, rank, uid[0])
+            fn = lambda *a: ep.moe_prefill_ep_nccl(*a, comm)
         if mode == "ag2":    # pipelined over two slices of the tokens, GEMMs on 132 SMs
             import _lib
             _lib.set_prefill_sm_budget(132)
@@ -56,13 +62,15 @@ def _worker(rank, port, results, mode="a2a"):
                  torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0, shard)
         torch.cuda.synchronize()
         results[rank] = out.cpu().numpy()
+        if comm is not None:
+            comm.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["a2a", "ag", "ag2"])
+@pytest.mark.parametrize("mode", ["a2a", "ag", "ag2", "nccl_c"])
 def test_expert_parallel_prefill_two_gpus_matches_oracle(mode):
     """a2a: all-to-all dispatch/combine; ag: all-gather + reduce-scatter (pairs of
     the other rank's experts passed to the grouped GEMM as -1)."""
@@ -81,3 +89,25 @@ def test_expert_parallel_prefill_two_gpus_matches_oracle(mode):
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         out = np.concatenate([results[r] for r in range(WORLD)])
     assert rel_err(out, ref) <= 1e-4
+
+
+def test_c_abi_expert_parallel_layer_one_rank_matches_oracle():
+    """qfn_moe_prefill_ep over a one-rank NCCL communicator (the exchange
+    degenerates to copies; runs on a one-GPU box): all experts local."""
+    import ep
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    blocks, s2, x, ti, tv = _inputs()
+    comm = ep.NcclComm(1, 0, ep.NcclComm.unique_id())
+    try:
+        shard = ep.ExpertShard(E, 1, 0)
+        own = shard.experts
+        out = ep.moe_prefill_ep_nccl(x.to(dev), torch.from_numpy(ti).long().to(dev),
+                                     torch.from_numpy(tv).to(dev).to(torch.bfloat16),
+                                     torch.from_numpy(blocks[own]).to(dev), torch.from_numpy(s2[own]).to(dev), 0,
+                                     shard, comm)
+        torch.cuda.synchronize()
+    finally:
+        comm.close()
+    ref = oracle.moe_prefill(x.float().numpy(), ti, tv, blocks, 0, s2)
+    assert rel_err(out.cpu().numpy(), ref) <= 1e-4
