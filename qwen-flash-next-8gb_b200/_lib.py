@@ -76,6 +76,25 @@ def lib():
     return _lib
 
 
+_ops = None
+TORCH_EXT_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libqfn_torch.so")
+
+
+def ops():
+    """torch.ops.qfn: the thin torch extension over the C ABI (moe_decode,
+    moe_prefill, gemv).  Loads libqfn_torch.so (built next to libqfn.so by
+    build.py); there is no fallback when it is missing."""
+    global _ops
+    if _ops is None:
+        lib()   # libqfn.so first (the extension links it)
+        if not os.path.exists(TORCH_EXT_PATH):
+            raise RuntimeError(f"{TORCH_EXT_PATH} not built: run qwen-flash-next-8gb_b200/build.py "
+                               "(or __graft_entry__.build()); there is no non-CUDA fallback")
+        torch.ops.load_library(TORCH_EXT_PATH)
+        _ops = torch.ops.qfn
+    return _ops
+
+
 def check(rc, what):
     if rc != 0:
         L = lib()

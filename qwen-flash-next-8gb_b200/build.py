@@ -2,8 +2,9 @@
 
 Usage: python build.py [--force]
 
-The shared library is written next to this file so that it travels with the
-source tree; `_lib.py` loads it from there.  Rebuilds only when a source or
+The shared library (and the thin torch extension over it, libqfn_torch.so)
+is written next to this file so that it travels with the source tree;
+`_lib.py` loads it from there.  Rebuilds only when a source or
 header is newer than the library (or with --force).
 """
 import os
@@ -40,10 +41,42 @@ def needs_build():
     return any(os.path.getmtime(p) > t for p in deps())
 
 
+TORCH_EXT_SRC = os.path.join(HERE, "torch_ext", "qfn_torch.cpp")
+TORCH_EXT = os.path.join(HERE, "libqfn_torch.so")
+
+
+def build_torch_ext(force=False):
+    """The thin torch extension (torch.ops.qfn.*) over libqfn.so, compiled with
+    g++ against the installed torch; linked to libqfn.so next to it."""
+    deps_ = [TORCH_EXT_SRC, LIB, os.path.join(INCLUDE, "qfn.h")]
+    if not force and os.path.exists(TORCH_EXT) and all(os.path.getmtime(p) <= os.path.getmtime(TORCH_EXT)
+                                                       for p in deps_):
+        return TORCH_EXT
+    import torch
+    import torch.utils.cpp_extension as ce
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    inc = [f"-I{p}" for p in ce.include_paths()] + ["-I/usr/local/cuda/include", f"-I{INCLUDE}"]
+    libs = [f"-L{p}" for p in ce.library_paths()] + ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu"]
+    tmp = TORCH_EXT + ".tmp"
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *inc, TORCH_EXT_SRC,
+           *libs, f"-L{HERE}", "-lqfn", "-Wl,-rpath,$ORIGIN", "-o", tmp]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ (torch extension) failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TORCH_EXT)
+    return TORCH_EXT
+
+
 def build(force=False, verbose=False):
-    """Compile every .cu under csrc/ into libqfn.so; returns the library path."""
-    if not force and not needs_build():
-        return LIB
+    """Compile every .cu under csrc/ into libqfn.so, then the torch extension
+    over it (libqfn_torch.so); returns the library path."""
+    if force or needs_build():
+        _build_lib(verbose)
+    build_torch_ext(force)
+    return LIB
+
+
+def _build_lib(verbose=False):
     tmp = LIB + ".tmp"
     cmd = [NVCC, *ARCH, *FLAGS, *sources(), "-o", tmp, "-lcuda", "-ldl"]
     if verbose:
@@ -55,7 +88,6 @@ def build(force=False, verbose=False):
     if verbose:
         print(r.stdout + r.stderr)
     os.replace(tmp, LIB)
-    return LIB
 
 
 if __name__ == "__main__":

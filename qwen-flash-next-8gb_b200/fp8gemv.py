@@ -16,26 +16,13 @@ and the same bf16 GEMM.
 import torch
 import torch.nn.functional as F
 
-from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, on_device, stream_of
+from _lib import DTYPE_BF16, DTYPE_F32, check, lib, ops, require_cuda, on_device, stream_of
 
 
 def _gemv(q, s, x, out_dtype):
-    require_cuda("q", q)
-    if q.dtype not in (torch.float8_e4m3fn, torch.uint8):
-        raise TypeError(f"q must be float8_e4m3fn (or its raw uint8 bytes), got {q.dtype}")
-    require_cuda("s", s, torch.float32)
-    require_cuda("x", x, torch.bfloat16)
-    if q.dim() != 2:
-        raise ValueError("q must be [N, K]")
-    N, K = q.shape
-    if s.numel() != N or x.numel() != K:
-        raise ValueError(f"s must have {N} and x {K} elements; got {s.numel()}, {x.numel()}")
-    y = torch.empty(N, dtype=out_dtype, device=q.device)
-    with on_device(q.device):
-        rc = lib().qfn_gemv_e4m3(q.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(),
-                                 DTYPE_F32 if out_dtype == torch.float32 else DTYPE_BF16, N, K, stream_of(y))
-    check(rc, "qfn_gemv_e4m3")
-    return y
+    """The torch operator qfn::gemv (libqfn_torch.so -> qfn_gemv_e4m3): checks
+    the tensors, launches on torch's current stream."""
+    return ops().gemv(q, s, x, out_dtype == torch.float32)
 
 
 def gemv(q, s, x):

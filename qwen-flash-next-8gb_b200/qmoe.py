@@ -13,7 +13,7 @@ import ctypes
 
 import torch
 
-from _lib import DTYPE_BF16, DTYPE_F32, check, lib, require_cuda, on_device, stream_of
+from _lib import DTYPE_BF16, DTYPE_F32, check, lib, ops, require_cuda, on_device, stream_of
 
 HID, INTER = 2560, 640
 BLOCK = 2764800
@@ -50,37 +50,10 @@ VARIANT_AUTO, VARIANT_CUDA_CORE, VARIANT_SLICE = 0, 2, 4
 
 
 def _moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant):
-    """moe_decode with an explicit kernel path (tests / measurements)."""
-    require_cuda("slots_u8", slots_u8, torch.uint8)
-    require_cuda("sidx", sidx, torch.int32)
-    require_cuda("s2", s2, torch.float32)
-    require_cuda("coef", coef, torch.float32)
-    require_cuda("x", x)
-    require_cuda("h_buf", h_buf, torch.float32)
-    K = sidx.shape[0]
-    if slots_u8.dim() != 2 or slots_u8.shape[1] != BLOCK:
-        raise ValueError(f"slots_u8 must be [S, {BLOCK}], got {tuple(slots_u8.shape)}")
-    if sidx.dim() != 1 or not 1 <= K <= MAX_TOPK:
-        raise ValueError(f"sidx must be int32[K] with 1 <= K <= {MAX_TOPK}")
-    if tuple(s2.shape) != (K, 3) or tuple(coef.shape) != (K,):
-        raise ValueError(f"s2 must be [K,3] and coef [K]; got {tuple(s2.shape)}, {tuple(coef.shape)}")
-    if x.numel() != HID or x.dtype not in (torch.bfloat16, torch.float32):
-        raise ValueError(f"x must be bf16/fp32 with {HID} elements")
-    if h_buf.dim() != 2 or h_buf.shape[0] < K or h_buf.shape[1] != INTER:
-        raise ValueError(f"h_buf must be f32[>=K, {INTER}]")
-    dev = slots_u8.device
-    di = slots_u8.get_device()
-    for name, t in (("sidx", sidx), ("s2", s2), ("coef", coef), ("x", x), ("h_buf", h_buf)):
-        if t.get_device() != di:
-            raise ValueError(f"{name} is on {t.device}, slots_u8 on {dev}")
-    out = torch.empty(HID, dtype=torch.float32, device=dev)
-    with on_device(dev):
-        rc = lib().qfn_moe_decode_variant(slots_u8.data_ptr(), slots_u8.shape[0], sidx.data_ptr(),
-                                          s2.data_ptr(), coef.data_ptr(), x.data_ptr(),
-                                          DTYPE_F32 if x.dtype == torch.float32 else DTYPE_BF16,
-                                          h_buf.data_ptr(), out.data_ptr(), K, variant, stream_of(out))
-    check(rc, "qfn_moe_decode")
-    return out
+    """moe_decode with an explicit kernel path (tests / measurements): one call
+    of the torch operator qfn::moe_decode (libqfn_torch.so -> qfn_moe_decode_variant),
+    which checks the tensors and launches on torch's current stream."""
+    return ops().moe_decode(slots_u8, sidx, s2, coef, x, h_buf, variant)
 
 
 def moe_prefill(x, ti, tv, table, s2, L=0):
@@ -93,44 +66,10 @@ def moe_prefill(x, ti, tv, table, s2, L=0):
     [T, 2560] = sum_k tv[t,k] * down_e(silu(gate_e x_t) * up_e x_t), the
     reference's `out` before its cast to bf16.  One call replaces the whole
     per-expert loop (and its host syncs): grouped tcgen05 GEMMs on the GPU.
-    Queued on torch's current stream; graph-capturable.
+    Queued on torch's current stream; graph-capturable (the torch operator
+    qfn::moe_prefill allocates its workspace from torch's caching allocator).
     """
-    require_cuda("x", x, torch.bfloat16)
-    require_cuda("ti", ti)
-    require_cuda("tv", tv)
-    require_cuda("table", table, torch.uint8)
-    require_cuda("s2", s2, torch.float32)
-    if x.dim() != 2 or x.shape[1] != HID:
-        raise ValueError(f"x must be bf16[T, {HID}], got {tuple(x.shape)}")
-    T = x.shape[0]
-    if ti.dim() != 2 or ti.shape[0] != T or tuple(tv.shape) != tuple(ti.shape):
-        raise ValueError(f"ti and tv must be [T, topk] with T={T}; got {tuple(ti.shape)}, {tuple(tv.shape)}")
-    if ti.dtype not in (torch.int64, torch.int32):
-        raise TypeError("ti must be int64 or int32")
-    if tv.dtype not in (torch.bfloat16, torch.float32):
-        raise TypeError("tv must be bf16 or fp32")
-    if s2.dim() != 2 or s2.shape[1] != 3:
-        raise ValueError(f"s2 must be f32[n_experts, 3], got {tuple(s2.shape)}")
-    if table.dim() != 2 or table.shape[1] != BLOCK:
-        raise ValueError(f"table must be [NB, {BLOCK}]")
-    dev = x.device
-    for name, t in (("ti", ti), ("tv", tv), ("table", table), ("s2", s2)):
-        if t.device != dev:
-            raise ValueError(f"{name} is on {t.device}, x on {dev}")
-    topk, E = ti.shape[1], s2.shape[0]
-    out = torch.empty(T, HID, dtype=torch.float32, device=dev)
-    if T == 0:
-        return out
-    L_ = lib()
-    nbytes = L_.qfn_moe_prefill_workspace(T, topk, E)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    with on_device(dev):
-        rc = L_.qfn_moe_prefill(x.data_ptr(), T, ti.data_ptr(), int(ti.dtype == torch.int64), tv.data_ptr(),
-                                DTYPE_BF16 if tv.dtype == torch.bfloat16 else DTYPE_F32, topk, table.data_ptr(),
-                                table.shape[0], int(L) * E, s2.data_ptr(), E, out.data_ptr(), ws.data_ptr(),
-                                nbytes, stream_of(out))
-    check(rc, "qfn_moe_prefill")
-    return out
+    return ops().moe_prefill(x, ti, tv, table, s2, int(L))
 
 
 def deq(w_u8, s_e4m3_u8, ws2):
