@@ -55,6 +55,9 @@ constexpr int kPfDeqSplit = kPfDeq / 8;
 constexpr int kPfEpi0 = 4 + kPfDeq;                 // first epilogue warp
 constexpr int kPfThreads = 32 * (kPfEpi0 + 4);
 constexpr int kPfMaxExperts = 1024;
+constexpr int kPfJobQ = 8;                           // job-queue slots (jobs handed to the roles ahead of use)
+constexpr int kPfJobAhead = 2;                       // jobs warp 0 publishes beyond the one it works on
+constexpr uint32_t kPfJobReaders = 2 + kPfDeq + 4;   // warps that read each job: MMA, weights, dequantisers, epilogue
 constexpr unsigned kPfStatusTimeout = 1u, kPfStatusBadExpert = 4u;
 
 __device__ unsigned int g_prefill_status = 0;
@@ -173,6 +176,8 @@ __global__ void __launch_bounds__(1024) pf_plan_kernel(const int* __restrict__ h
     offs[E] = np;
     hdr[0] = nt;
     hdr[1] = np;
+    hdr[2] = 0;   // the job counters of the two GEMMs
+    hdr[3] = 0;
   }
 }
 
@@ -455,6 +460,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* js_empty = js_full + 2;  // [2] the dequant warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(js_empty + 2);
   volatile uint32_t* abort = tslot + 1;
+  // job queue: warp 0 takes job indices from the call's counter and hands
+  // them to the other roles through a ring of kPfJobQ slots
+  uint64_t* jq_full = reinterpret_cast<uint64_t*>(tslot + 2);
+  uint64_t* jq_empty = jq_full + kPfJobQ;
+  int* jq_ids = reinterpret_cast<int*>(jq_empty + kPfJobQ);
   int* cols = reinterpret_cast<int*>(smem + L::kCols);  // [2][2][128]: per-column factors (epilogue)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -473,6 +483,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&tm_empty[h], 4);
       mbar_init(&js_full[h], 1);
       mbar_init(&js_empty[h], 1);
+    }
+    for (int q = 0; q < kPfJobQ; ++q) {
+      mbar_init(&jq_full[q], 1);
+      mbar_init(&jq_empty[q], kPfJobReaders);
     }
     fence_mbar_init();
   }
@@ -494,14 +508,58 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   pdl_wait();
   pdl_launch_dependents();
   const int n_jobs = args.hdr[0] * C::kSub;
+  // Gate/up jobs are handed out dynamically (an atomic counter in the
+  // workspace header, zeroed by the plan kernel): a CTA whose jobs ran fast
+  // takes more, so the CTAs finish together instead of each running a fixed
+  // 1/grid of the jobs (measured: the slowest CTA ended 327 us after the
+  // start against 309 us); every role walks the same sequence from the ring.
+  // Down jobs are dealt statically (job blockIdx.x + q * grid), which measured
+  // faster for them (286 against 301 us).
+  int* const job_ctr = const_cast<int*>(args.hdr) + 2 + MODE;
+  auto publish_job = [&](int q) -> int {   // warp 0, all lanes: the q-th job of this CTA (-1: none left)
+    if (MODE == kDown) {   // down jobs (a few us each) measured faster dealt statically: 1/grid of the jobs per CTA
+      const int u = static_cast<int>(blockIdx.x) + q * static_cast<int>(gridDim.x);
+      if (lane == 0) jq_ids[q % kPfJobQ] = u < n_jobs ? u : -1;
+      return u < n_jobs ? u : -1;
+    }
+    const int slot = q % kPfJobQ;
+    if (!pf_wait(&jq_empty[slot], ((q / kPfJobQ) & 1) ^ 1, abort)) return -1;
+    int u = -1;
+    if (lane == 0) {
+      u = atomicAdd(job_ctr, 1);
+      if (u >= n_jobs) u = -1;
+      jq_ids[slot] = u;
+      mbar_arrive(&jq_full[slot]);
+    }
+    return __shfl_sync(0xffffffffu, u, 0);
+  };
+  auto next_job = [&](int q) -> int {      // a reading warp, all lanes
+    if (MODE == kDown) {
+      const int u = static_cast<int>(blockIdx.x) + q * static_cast<int>(gridDim.x);
+      return u < n_jobs && !*abort ? u : -1;
+    }
+    const int slot = q % kPfJobQ;
+    if (!pf_wait(&jq_full[slot], (q / kPfJobQ) & 1, abort)) return -1;
+    const int u = *reinterpret_cast<volatile int*>(&jq_ids[slot]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&jq_empty[slot]);
+    return u;
+  };
 
   if (warp == 0) {
     // ---------------- activation producer (warp 0; one elected lane issues):
     // per stage the tile's activation rows of two K-blocks (down: h hi and
     // h lo per K-block) in the smallest box that holds them, completing on
     // the stage's k_full barrier.
-    int st = 0;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
+    int st = 0, pub = 0;
+    bool fin = false;
+    for (int jq = 0;; ++jq) {
+      // keep kPfJobAhead jobs published beyond this one (the counter's atomic
+      // round trip then stays off the path between two jobs)
+      while (!fin && pub <= jq + kPfJobAhead) fin = publish_job(pub++) < 0;
+      __syncwarp();
+      const int u = *reinterpret_cast<volatile int*>(&jq_ids[jq % kPfJobQ]);
+      if (u < 0 || *abort) break;
       const int t = u / C::kSub;
       const int p0 = args.tile_p0[t], hb = pf_box(args.tile_n[t]);
       const uint32_t bbytes = (16u << hb) * 128u;
@@ -531,7 +589,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // 128 scale rows.  (An L2 prefetch of the next job's rows measured
     // slower: with the activation rows it overflows L2 and doubles DRAM reads.)
     int rt = 0, jj = 0;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
+    for (int jq = 0;; ++jq, ++jj) {
+      const int u = next_job(jq);
+      if (u < 0) break;
       const int t = u / C::kSub, sub = u % C::kSub;
       const int blk = static_cast<int>(args.base + args.tile_e[t]);
       if (MODE == kDown) {  // the job's scale rows: [64 row pairs][80 B]
@@ -569,7 +629,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     constexpr int NG = MODE == kGateUp ? 2 : 1;
     int st = 0;
     PfHalves<MODE> hv;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x) {
+    for (int jq = 0;; ++jq) {
+      const int u = next_job(jq);
+      if (u < 0) break;
       const int n = args.tile_n[u / C::kSub];
       const int hb = pf_box(n), rows = 16 << hb;
       const uint32_t bbytes = static_cast<uint32_t>(rows) * 128u;
@@ -642,7 +704,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     constexpr int NV = MODE == kGateUp ? 32 : 16;  // f16x2 words per K-block and thread
     int st = 0, jj = 0;
     uint4 sc = make_uint4(0, 0, 0, 0);
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
+    for (int jq = 0;; ++jq, ++jj) {
+      const int u = next_job(jq);
+      if (u < 0) break;
       const uint8_t* jsc = smem + L::kJs + (jj & 1) * C::kJobScales + r * (kInter / 16);
       if (MODE == kDown) pf_wait(&js_full[jj & 1], (jj >> 1) & 1, abort);
       for (int q = 0; q < NST; ++q, ++st) {
@@ -722,7 +786,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int et = threadIdx.x - 32 * kPfEpi0;  // 0..127
     int jj = 0;
     PfHalves<MODE> hv;
-    for (int u = blockIdx.x; u < n_jobs; u += gridDim.x, ++jj) {
+    for (int jq = 0;; ++jq, ++jj) {
+      const int u = next_job(jq);
+      if (u < 0) break;
       const int t = u / C::kSub, sub = u % C::kSub;
       const int e = args.tile_e[t], p0 = args.tile_p0[t], n = args.tile_n[t];
       // per-column factors of the job: gate/up: ws2_g 2^-ex, ws2_u 2^-ex;
