@@ -68,10 +68,10 @@ LIN_COPIES = 4
 # record, from ncu captures of the same shapes (None: not captured).
 TRAFFIC = {
     "decode": 27.72e6,              # moe_decode_slice, one layer (K = 10)
-    "prefill": 1.7508e9,            # pf_gemm<0> + pf_gemm<1>, one config-3 layer
-    "gemv_ratio": 31.554816e6 / 31.536128e6,   # gemv_stream_kernel (12288 x 2560) DRAM bytes / algorithmic bytes
+    "prefill": 1.7469e9,            # pf_gemm<0> + pf_gemm<1>, one config-3 layer
+    "gemv_ratio": 31.555328e6 / 31.536128e6,   # gemv_stream_kernel (12288 x 2560) DRAM bytes / algorithmic bytes
     # route logits + select + moe_decode_slice + shared gate/up + down, one layer
-    "decode_block": 2.635e6 + 0.064e6 + 27.72e6 + 6.581e6 + 3.289e6,
+    "decode_block": 2.635e6 + 0.023e6 + 27.72e6 + 6.581e6 + 3.299e6,
     # deltanet_step_kernel: the state's reads (its writes reach DRAM from L2 after the launch)
     "deltanet": 2.140e6,
 }
