@@ -1010,9 +1010,11 @@ def decode_block_record(ctx, steps):
     routers = [(torch.randn(N_EXPERTS, HID, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(L)]
     shared = [tuple((torch.randn(*shp, device=dev, generator=g) * 0.02).to(torch.bfloat16)
                     for shp in ((SH_INTER, HID), (SH_INTER, HID), (HID, SH_INTER), (1, HID))) for _ in range(L)]
-    xs = [torch.randn(1, HID, device=dev, generator=g).to(torch.bfloat16) for _ in range(L)]
+    x_all = torch.randn(L, 1, HID, device=dev, generator=g).to(torch.bfloat16)
+    xs = list(x_all)                        # the layers' inputs: views of one buffer
     blk = moe_block.DecodeMoE(table, topk=TOPK)
-    outs = [torch.empty(1, HID, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    out_all = torch.empty(L, 1, HID, dtype=torch.bfloat16, device=dev)
+    outs = list(out_all)
 
     def step():
         for l in range(L):
@@ -1045,19 +1047,23 @@ def decode_block_record(ctx, steps):
     parity["pass"] = parity["max_err_rms"] <= 1e-2 and parity["argmax_equal"]
     parity["checker"] = "oracle router + moe_decode + shared expert (bf16 output: a few bf16 steps)"
 
-    # e2e: x of every layer from pinned host memory, every layer's bf16 output back, one graph
-    h_x = torch.stack(xs).cpu().pin_memory()
-    h_out = torch.empty(L, 1, HID, dtype=torch.bfloat16).pin_memory()
-    d_x = torch.stack(xs)
+    # e2e: x of every layer from pinned host memory and every layer's bf16 output
+    # back each step, steps pipelined over two buffer sets (the next step's x
+    # and the previous step's outputs copy on two copy streams during the graph)
+    h_x = x_all.cpu().pin_memory()
+    h_out = [torch.empty(L, 1, HID, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    d_x = [torch.empty_like(x_all) for _ in range(2)]
+    d_o = [torch.empty_like(out_all) for _ in range(2)]
 
-    def e2e_step(i):
-        d_x.copy_(h_x, non_blocking=True)
-        for l_ in range(L):
-            xs[l_].copy_(d_x[l_])
+    def e2e_compute(i, k):
+        x_all.copy_(d_x[k])
         gr.replay()
-        h_out.copy_(torch.stack(outs), non_blocking=True)
+        return d_o[k].copy_(out_all)
 
-    ms_e2e = ctx.timed(e2e_step, min(args.e2e_steps, steps), 2)
+    e2e_pipelined = make_e2e_pipeline(lambda i, k: d_x[k].copy_(h_x, non_blocking=True), e2e_compute,
+                                      lambda i, k, o: h_out[k].copy_(o, non_blocking=True))
+    E = min(args.e2e_steps, steps)
+    ms_e2e = ctx.timed(lambda i: e2e_pipelined(E), 1, 2) / E
     hbm, _, kind = peaks()
     achieved = layer_bytes * L / (ms * 1e-3) / 1e9
     if not parity["pass"]:
@@ -1072,7 +1078,8 @@ def decode_block_record(ctx, steps):
                    "l2": "no flush: each step streams > 1.3 GB of distinct expert bytes (> 126 MB L2)"},
         "e2e": {"value": ms_e2e * 1e3 / L, "unit": "us/layer", "h2d_bytes_per_step": L * HID * 2,
                 "d2h_bytes_per_step": L * HID * 2, "ms_per_step": ms_e2e,
-                "path": "moe_block.DecodeMoE per layer (router, routed experts, shared expert) in one CUDA graph; "
+                "path": "moe_block.DecodeMoE per layer (router, routed experts, shared expert) in one CUDA graph, "
+                        "steps pipelined over two buffer sets (copies on two copy streams); "
                         "x in from and bf16 outputs out to pinned host memory"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "traffic": TRAFFIC["decode_block"],
@@ -1138,6 +1145,34 @@ def deltanet_record(ctx, steps):
     if not parity["pass"]:
         ctx.failed.append("deltanet")
     del gr
+
+    # e2e: per step every layer's q, k, v, g, beta from pinned host memory and
+    # its output back, steps pipelined over two buffer sets inside one CUDA graph
+    h_in = [t.cpu().pin_memory() for t in (q, k, v, g, beta)]
+    d_in = [[torch.empty_like(t) for t in (q, k, v, g, beta)] for _ in range(2)]
+
+    def e2e_compute(i, kk):
+        dq, dk_, dv_, dg, db = d_in[kk]
+        return torch.stack([deltanet.recurrent_gated_delta_rule(dq[l][None, None], dk_[l][None, None],
+                                                                dv_[l][None, None], dg[l][None, None],
+                                                                db[l][None, None], S[l])[0] for l in range(L)])
+
+    probe = e2e_compute(0, 0)
+    h_out = [torch.empty(probe.shape, dtype=probe.dtype).pin_memory() for _ in range(2)]
+    e2e_pipelined = make_e2e_pipeline(
+        lambda i, kk: [d.copy_(h, non_blocking=True) for d, h in zip(d_in[kk], h_in)],
+        e2e_compute,
+        lambda i, kk, o: h_out[kk].copy_(o, non_blocking=True))
+    E = 16
+    e2e_pipelined(2)
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_pipelined(E)
+    ms_e2e = ctx.timed(lambda i: e2e_graph.replay(), 4, 2) / E
+    del e2e_graph
+    h2d = sum(t.numel() * t.element_size() for t in h_in)
+    d2h = probe.numel() * probe.element_size()
     return {
         "metric": "DeltaNet one-token state update us/layer (32 heads, 128 x 128 fp32 state)", "value": ms * 1e3 / L,
         "unit": "us/layer", "higher_is_better": False, "ms_per_step": ms, "steps": steps,
@@ -1145,6 +1180,11 @@ def deltanet_record(ctx, steps):
                                f"dv {dv}; one CUDA graph per step", "layer_bytes": layer_bytes,
                    "l2": f"no flush: {L} states of {state_bytes / 2 / 1e6:.1f} MB = {L * state_bytes / 2e6:.0f} MB "
                          "per step (> 126 MB L2 with reads and writes)"},
+        "e2e": {"value": ms_e2e * 1e3 / L, "unit": "us/layer", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": ms_e2e,
+                "path": "deltanet.recurrent_gated_delta_rule per layer (public API) with pinned host q, k, v, g, beta "
+                        "in and the bf16 outputs out every step, steps pipelined over two buffer sets (copies on two "
+                        f"copy streams), {E} steps per CUDA graph"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": kind, "traffic": TRAFFIC["deltanet"], "kernel": "deltanet_step_kernel"},
         "parity": parity,
