@@ -184,3 +184,17 @@ def test_prefill_validation_and_workspace_size():
     assert call(wsb=ws - 1) == 5                 # workspace too small
     assert call(ws=ctypes.c_void_p(0x10010)) == 2  # workspace not 256-byte aligned
 
+
+def test_torch_extension_registers_the_hot_path_operators():
+    """libqfn_torch.so (the thin torch extension over the C ABI) loads on a
+    machine without a GPU and registers the three operators; a CPU tensor is
+    refused by the operator's own checks."""
+    import torch
+    ops = _lib.ops()
+    for name in ("moe_decode", "moe_prefill", "gemv"):
+        assert hasattr(ops, name), name
+    schema = str(torch.ops.qfn.moe_decode.default._schema)
+    assert "Tensor(a!) h_buf" in schema and "int variant" in schema
+    with pytest.raises(ValueError, match="CUDA"):
+        torch.ops.qfn.gemv(torch.zeros(16, 32, dtype=torch.uint8), torch.ones(16), torch.zeros(32, dtype=torch.bfloat16),
+                           False)
