@@ -1,7 +1,9 @@
-"""ctypes binding of libqfn.so, the C ABI declared in include/qfn.h.
+"""Bindings of libqfn.so, the C ABI declared in include/qfn.h: ctypes for every
+entry point (lib()), and the thin torch extension over the same ABI for the
+three hot-path operators (ops(): torch.ops.qfn.moe_decode / moe_prefill / gemv).
 
-The library is loaded from this directory (built in-tree by build.py).  There
-is no fallback: if the library is missing or the device is not an sm_100
+Both libraries are loaded from this directory (built in-tree by build.py).
+There is no fallback: if a library is missing or the device is not an sm_100
 part, every call raises.
 """
 import contextlib

@@ -25,11 +25,11 @@
 //     the epilogue sums the two column blocks: ~22-bit h), and adds
 //     coef * ws2_d * D into out with fp32 atomics (as index_add_ on CUDA).
 //
-// pf_gemm is persistent (one CTA per SM) and warp-specialised: warp 0 issues
-// TMA loads (activation tiles, raw e2m1 rows) into a ring of stages; warps
-// 4-11 dequantise the raw rows of each stage into two f16 A tiles (their
-// scale rows stream from global memory ahead of use); one thread of warp 1
-// issues the MMAs; warps 12-15 drain the TMEM accumulators (two sets, so the
+// pf_gemm is persistent (one CTA per SM) and warp-specialised: warp 0 loads
+// the activation tiles (TMA) into a ring of stages and hands out the jobs;
+// warp 3 loads the raw e2m1 rows and their scales; warps 4-19 dequantise the
+// raw rows of each stage into the f16 A operand in TMEM; one thread of warp 1
+// issues the MMAs; warps 20-23 drain the TMEM accumulators (two halves, so the
 // epilogue of one job overlaps the next job's MMAs).  Every wait is bounded;
 // a wait that runs out sets a status bit.
 #include <cuda_fp16.h>
