@@ -152,9 +152,10 @@ int qfn_moe_decode_noalloc(const uint8_t* table, int64_t n_blocks, const int32_t
                            float* out, int K, qfn_stream_t stream);
 
 /*
- * qfn_device_status -- read (and with clear != 0, reset) the decode kernels'
- * device status word of the current device: bit 0 = a bounded wait on a
- * shared-memory barrier ran out (the outputs of that call are invalid).
+ * qfn_device_status -- read (and with clear != 0, reset) the device status
+ * words of the decode, GEMV and FP8 linear kernels of the current device,
+ * OR-ed: bit 0 = a bounded wait on a shared-memory barrier ran out (the
+ * outputs of that call are invalid).
  * Synchronous (a device-to-host copy).  No counterpart in the reference,
  * whose kernels have no waits.
  */
@@ -267,6 +268,22 @@ int qfn_gemv_e4m3(const uint8_t* q, const float* s, const uint16_t* x, void* y,
  */
 int qfn_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* w, int64_t N, int64_t K,
                           qfn_stream_t stream);
+
+/*
+ * qfn_linear_e4m3 -- replaces the engine's FP8 linear layer for T > 1 tokens,
+ * Lin.__call__ (qwen_engine.py:79-83): F.linear(x, (q.to(bf16) * s).to(bf16)).
+ *   y[t][n] = bf16_rn( sum_k x[t][k] * w[n][k] ),  fp32 accumulation,
+ *   w[n][k] = bf16_rn(fp32(e4m3(q[n][k])) * s[n])  (the weights of
+ *   qfn_e4m3_rows_to_bf16, formed on chip; never written to memory).
+ *   q: u8[N][K] (float8_e4m3fn bytes) device, 16-byte aligned, K % 16 == 0.
+ *   s: f32[N] device.  x: bf16[T][K] device, 16-byte aligned.
+ *   y: bf16[T][N] device.  T, N, K < 2^30.
+ * One launch (a programmatic dependent of the previous kernel in the
+ * stream).  Results differ from a library GEMM only by the fp32 summation
+ * order (at most one bf16 step).
+ */
+int qfn_linear_e4m3(const uint8_t* q, const float* s, const uint16_t* x, uint16_t* y, int64_t T,
+                    int64_t N, int64_t K, qfn_stream_t stream);
 
 /*
  * qfn_moe_prefill -- the batched-prefill expert loop of QwenEngine.moe

@@ -1,6 +1,7 @@
 """Bindings of libqfn.so, the C ABI declared in include/qfn.h: ctypes for every
 entry point (lib()), and the thin torch extension over the same ABI for the
-three hot-path operators (ops(): torch.ops.qfn.moe_decode / moe_prefill / gemv).
+hot-path operators (ops(): torch.ops.qfn.moe_decode / moe_prefill / gemv /
+linear).
 
 Both libraries are loaded from this directory (built in-tree by build.py).
 There is no fallback: if a library is missing or the device is not an sm_100
@@ -32,6 +33,7 @@ SIGNATURES = {
     "qfn_device_status": [_P, _I],
     "qfn_gemv_e4m3": [_P, _P, _P, _P, _I, _I64, _I64, _P],
     "qfn_e4m3_rows_to_bf16": [_P, _P, _P, _I64, _I64, _P],
+    "qfn_linear_e4m3": [_P, _P, _P, _P, _I64, _I64, _I64, _P],
     "qfn_moe_prefill_workspace": [_I64, _I, _I],
     "qfn_moe_prefill": [_P, _I64, _P, _I, _P, _I, _I, _P, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P],
     "qfn_prefill_status": [_P, _I],
@@ -84,7 +86,7 @@ TORCH_EXT_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libqf
 
 def ops():
     """torch.ops.qfn: the thin torch extension over the C ABI (moe_decode,
-    moe_prefill, gemv).  Loads libqfn_torch.so (built next to libqfn.so by
+    moe_prefill, gemv, linear).  Loads libqfn_torch.so (built next to libqfn.so by
     build.py); there is no fallback when it is missing."""
     global _ops
     if _ops is None:

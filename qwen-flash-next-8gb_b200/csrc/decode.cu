@@ -356,7 +356,12 @@ extern "C" int qfn_device_status(unsigned int* status, int clear) {
     e = cudaMemcpyToSymbol(g_decode_status, &zero, sizeof(unsigned int));
   }
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "qfn_device_status: %s", cudaGetErrorString(e));
-  return QFN_OK;
+  // the GEMV's and the FP8 linear layer's words (same bit meanings)
+  unsigned int g = 0, l = 0;
+  int rc = gemv_status(&g, clear != 0);
+  if (rc == QFN_OK) rc = linear_status(&l, clear != 0);
+  *status |= g | l;
+  return rc;
 }
 
 // ---------------------------------------------------------------------------

@@ -423,6 +423,15 @@ static int launch_e4m3_rows_to_bf16(const uint8_t* q, const float* s, uint16_t* 
   return check_launch("e4m3_rows_to_bf16_kernel");
 }
 
+int gemv_status(unsigned int* v, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(v, g_gemv_status, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(unsigned int));
+  }
+  return e == cudaSuccess ? QFN_OK : set_error(QFN_ERR_CUDA, "gemv status: %s", cudaGetErrorString(e));
+}
+
 }  // namespace qfn
 
 using namespace qfn;

@@ -32,6 +32,11 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 // Check the launch that was just queued.
 int check_launch(const char* what);
 
+// Read (clear != false: and reset) the status words of the GEMV and of the
+// FP8 linear layer on the current device (bit 0: a bounded wait ran out).
+int gemv_status(unsigned int* v, bool clear);
+int linear_status(unsigned int* v, bool clear);
+
 }  // namespace qfn
 
 #define QFN_REQUIRE(cond, status, ...)                 \

@@ -9,12 +9,12 @@ reference's DeltaNet graphs require (qwen_delta_graph.py:55-57).
 
 linear(x, q, s) is the engine's FP8 linear layer (Lin.__call__,
 qwen_engine.py:79-83) for any number of tokens: the GEMV for one token, and
-for T > 1 the reference's F.linear(x, (q.to(bf16) * s).to(bf16)) with the
-weight expression computed by one libqfn kernel (bit-identical bf16 weights)
-and the same bf16 GEMM.
+for T > 1 the reference's F.linear(x, (q.to(bf16) * s).to(bf16)) as one
+libqfn GEMM that forms the bf16 weights on chip (csrc/linear.cu).
+dequant_bf16(q, s) keeps the weight expression alone (bit-identical bf16
+weights in memory).
 """
 import torch
-import torch.nn.functional as F
 
 from _lib import DTYPE_BF16, DTYPE_F32, check, lib, ops, require_cuda, on_device, stream_of
 
@@ -62,10 +62,13 @@ def dequant_bf16(q, s):
 def linear(x, q, s):
     """Lin.__call__ of an FP8 layer (qwen_engine.py:79-83): x [T,K] bf16 -> [T,N] bf16.
 
-    T == 1: the GEMV (reads only the fp8 bytes); T > 1: F.linear with the
-    bf16 weights of dequant_bf16 (the reference's bf16 GEMM, same inputs)."""
-    if x.dim() != 2:
-        raise ValueError("x must be [T, K]")
+    T == 1: the GEMV (reads only the fp8 bytes).  T > 1: the torch operator
+    qfn::linear (-> qfn_linear_e4m3), one tcgen05 GEMM that forms the
+    reference's bf16 weights (q.to(bf16) * s).to(bf16) on chip from the fp8
+    bytes and accumulates in fp32, as F.linear on those weights does."""
+    if not isinstance(x, torch.Tensor) or x.dim() != 2:
+        raise ValueError("x must be a [T, K] tensor")
     if x.shape[0] == 1:
         return gemv(q, s.reshape(-1), x[0].contiguous())[None]
-    return F.linear(x, dequant_bf16(q, s))
+    require_cuda("x", x, torch.bfloat16, contiguous=False)
+    return ops().linear(x.contiguous(), q, s.reshape(-1).contiguous())

@@ -1,5 +1,5 @@
-// The thin torch extension over libqfn's C ABI: the three parts of the hot
-// path as torch operators (torch.ops.qfn.*), so that PyTorch callers reach the
+// The thin torch extension over libqfn's C ABI: the parts of the hot path
+// as torch operators (torch.ops.qfn.*), so that PyTorch callers reach the
 // kernels through one dispatcher call instead of ctypes.  Each operator
 // checks its tensors (type errors raise TypeError, shape / device errors
 // ValueError, as the Python wrappers did), makes the tensors' device current,
@@ -10,6 +10,7 @@
 //   qfn::moe_decode  -> qfn_moe_decode_variant  (qmoe.moe_decode, qmoe.py:77-83)
 //   qfn::moe_prefill -> qfn_moe_prefill         (the expert loop of QwenEngine.moe, qwen_engine.py:835-852)
 //   qfn::gemv        -> qfn_gemv_e4m3           (fp8gemv.gemv, fp8gemv.py:5-26)
+//   qfn::linear      -> qfn_linear_e4m3         (Lin.__call__ for T > 1, qwen_engine.py:79-83)
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -129,6 +130,33 @@ at::Tensor gemv(const at::Tensor& q, const at::Tensor& s, const at::Tensor& x, b
   return y;
 }
 
+// Lin.__call__ for T > 1 (qwen_engine.py:79-83): x [T, K] bf16 -> [T, N] bf16.
+at::Tensor linear(const at::Tensor& x, const at::Tensor& q, const at::Tensor& s) {
+  req_cuda(q, "q");
+  TORCH_CHECK_TYPE(q.scalar_type() == at::kFloat8_e4m3fn || q.scalar_type() == at::kByte,
+                   "q must be float8_e4m3fn (or its raw uint8 bytes), got ", q.scalar_type());
+  req_cuda(s, "s");
+  req_type(s, "s", at::kFloat);
+  req_cuda(x, "x");
+  req_type(x, "x", at::kBFloat16);
+  TORCH_CHECK_VALUE(q.dim() == 2 && x.dim() == 2, "q must be [N, K] and x [T, K]");
+  const int64_t N = q.size(0), K = q.size(1), T = x.size(0);
+  TORCH_CHECK_VALUE(x.size(1) == K && s.numel() == N, "x must be [T, ", K, "] and s have ", N, " elements; got ",
+                    x.sizes(), ", ", s.numel());
+  same_device(s, "s", q, "q");
+  same_device(x, "x", q, "q");
+  c10::cuda::CUDAGuard guard(q.device());
+  // the kernel's TMA reads x from a 16-byte aligned base (a view may start anywhere)
+  const at::Tensor xa = reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 ? x.clone() : x;
+  at::Tensor y = at::empty({T, N}, x.options());
+  if (T == 0 || N == 0) return y;
+  check_rc(qfn_linear_e4m3(static_cast<const uint8_t*>(q.data_ptr()), s.data_ptr<float>(),
+                           static_cast<const uint16_t*>(xa.data_ptr()), static_cast<uint16_t*>(y.data_ptr()), T, N, K,
+                           stream_of(y)),
+           "qfn_linear_e4m3");
+  return y;
+}
+
 }  // namespace
 
 // Catch-all kernels (not per dispatch key): a CPU tensor reaches the checks
@@ -138,4 +166,5 @@ TORCH_LIBRARY(qfn, m) {
         &moe_decode);
   m.def("moe_prefill(Tensor x, Tensor ti, Tensor tv, Tensor table, Tensor s2, int L) -> Tensor", &moe_prefill);
   m.def("gemv(Tensor q, Tensor s, Tensor x, bool out_f32) -> Tensor", &gemv);
+  m.def("linear(Tensor x, Tensor q, Tensor s) -> Tensor", &linear);
 }

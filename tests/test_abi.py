@@ -75,6 +75,13 @@ def test_validation_rejects_bad_arguments_without_touching_a_device():
     assert lib.qfn_gemv_e4m3(fake, fake, fake, fake, 1, 16, 24, None) == 4
     assert lib.qfn_gemv_e4m3(fake, fake, fake, fake, 5, 16, 32, None) == 1
     assert lib.qfn_gemv_e4m3(odd, fake, fake, fake, 1, 16, 32, None) == 2
+    # FP8 linear layer (T > 1): nulls, sizes, K % 16, alignment
+    ln = lambda q, x, T, N, K: lib.qfn_linear_e4m3(q, fake, x, fake, T, N, K, None)
+    assert ln(None, fake, 4, 16, 32) == 1
+    assert ln(fake, fake, 0, 16, 32) == 1
+    assert ln(fake, fake, 4, 16, 24) == 4
+    assert ln(odd, fake, 4, 16, 32) == 2
+    assert ln(fake, odd, 4, 16, 32) == 2
     # deq: K % 32
     assert lib.qfn_deq(fake, fake, ctypes.c_float(1.0), fake, 4, 48, None) == 4
     # e4m3 rows -> bf16: nulls, sizes, K % 16, alignment
@@ -187,11 +194,11 @@ def test_prefill_validation_and_workspace_size():
 
 def test_torch_extension_registers_the_hot_path_operators():
     """libqfn_torch.so (the thin torch extension over the C ABI) loads on a
-    machine without a GPU and registers the three operators; a CPU tensor is
+    machine without a GPU and registers the four operators; a CPU tensor is
     refused by the operator's own checks."""
     import torch
     ops = _lib.ops()
-    for name in ("moe_decode", "moe_prefill", "gemv"):
+    for name in ("moe_decode", "moe_prefill", "gemv", "linear"):
         assert hasattr(ops, name), name
     schema = str(torch.ops.qfn.moe_decode.default._schema)
     assert "Tensor(a!) h_buf" in schema and "int variant" in schema
