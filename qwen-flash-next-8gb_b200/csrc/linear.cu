@@ -8,28 +8,31 @@
 // K-block from the e4m3 bytes straight into TMEM, where they are the A
 // operand of tcgen05.mma kind::f16 (bf16 x bf16 -> fp32).
 //
-// Job = (128 weight rows, 256 tokens), dealt to the CTAs (one per SM, 448
+// Job = (128 weight rows, 256 tokens), dealt to the CTAs (one per SM, 480
 // threads) in the order row tile fastest, so that the CTAs running at one
 // time share the token tiles and walk the whole weight matrix through L2:
 //   warp 0       x producer: TMA boxes [256 tokens][64 k] (bf16, 128-byte
 //                swizzle) into a ring of kLnStages shared-memory stages;
 //   warp 1       MMA issuer: per K-block 4 k-steps x 2 accumulator halves
 //                (M = 128, N = 128 each; A from TMEM, B from shared memory);
-//   warps 2-9    converters, two groups of four warps taking alternate
-//                K-blocks: thread = weight row; its 64 e4m3 bytes of a
-//                K-block come from global memory (L2) into registers one of
-//                the group's K-blocks ahead, become bf16(fp32(q) * s) with
-//                the reference's two roundings, and go into one of
-//                kLnASlots TMEM A slots;
-//   warps 10-13  epilogue: TMEM -> RN bf16 -> y, each accumulator half
+//   warp 2       weight producer: TMA boxes [128 rows][64 B] of the e4m3
+//                bytes (64-byte swizzle) into a ring of kLnRawStages stages;
+//   warps 3-10   converters, two groups of four warps taking alternate
+//                K-blocks: thread = weight row; its 64 bytes of the K-block
+//                (four conflict-free 16-byte shared-memory reads) become
+//                bf16(fp32(q) * s) with the reference's two roundings and go
+//                into one of kLnASlots TMEM A slots;
+//   warps 11-14  epilogue: TMEM -> RN bf16 -> y, each accumulator half
 //                released as soon as it has been read.
 // TMEM: columns [0, 256) the accumulator (two halves of 128 tokens),
 // [256, 512) eight A slots of 32 columns (one K-block of 64 bf16 each).
 //
-// Why A in TMEM and the raw bytes through registers: with A in shared memory
-// a K-block would move 112 KB through shared memory (x in and out, raw
-// weights in and out, A in and out) against ~64 KB of bandwidth in the 512
-// cycles its MMAs take; this way it moves the 32 KB x tile in and out.
+// Why A in TMEM: from shared memory the A tiles would add 32 KB of shared
+// traffic per K-block (written by the converters, read by the MMAs) to the
+// x tile's 64 KB, in the 512 cycles the K-block's MMAs take.  The raw bytes
+// arrive by TMA: loaded by the converter threads themselves (a row per lane)
+// every warp load touched 32 L1 lines, and the converters stalled on them
+// (ncu: long-scoreboard 5.9 warps per issue, tensor pipe 40 % active).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -45,15 +48,18 @@ constexpr int kLnRows = 128;                          // weight rows per job (MM
 constexpr int kLnTok = 256;                           // tokens per job: two accumulator halves
 constexpr int kLnHalf = 128;                          // tokens per half (MMA N)
 constexpr int kLnKB = 64;                             // k per K-block
-constexpr int kLnStages = 6;                          // x ring stages
+constexpr int kLnStages = 5;                          // x ring stages
+constexpr int kLnRawStages = 6;                       // raw weight ring stages
 constexpr int kLnASlots = 8;                          // A slots in TMEM
 constexpr int kLnGroups = 2;                          // converter groups of four warps
-constexpr int kLnConv0 = 2;                           // first converter warp
+constexpr int kLnConv0 = 3;                           // first converter warp
 constexpr int kLnEpi0 = kLnConv0 + 4 * kLnGroups;     // first epilogue warp
-constexpr int kLnThreads = 32 * (kLnEpi0 + 4);        // 448
+constexpr int kLnThreads = 32 * (kLnEpi0 + 4);        // 480
 constexpr uint32_t kLnXBytes = kLnTok * kLnKB * 2;    // x tile per stage (32 KB)
+constexpr uint32_t kLnRawBytes = kLnRows * kLnKB;     // raw rows per stage (8 KB)
 constexpr uint32_t kLnTmemA = 256;                    // first A-slot column
-constexpr int kLnBar = kLnStages * static_cast<int>(kLnXBytes);
+constexpr int kLnRaw = kLnStages * static_cast<int>(kLnXBytes);
+constexpr int kLnBar = kLnRaw + kLnRawStages * static_cast<int>(kLnRawBytes);
 constexpr int kLnSmem = kLnBar + 512 + 1024;          // + barriers + alignment slack
 
 __device__ unsigned int g_linear_status = 0;
@@ -99,7 +105,8 @@ __device__ __forceinline__ void ln_convert16(uint4 v, float sc, uint32_t* o) {
   }
 }
 
-__global__ void __launch_bounds__(kLnThreads, 1) ln_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const LnArgs a) {
+__global__ void __launch_bounds__(kLnThreads, 1)
+    ln_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap, const LnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* ld_full = reinterpret_cast<uint64_t*>(smem + kLnBar);  // x tile landed (tx)
@@ -108,7 +115,9 @@ __global__ void __launch_bounds__(kLnThreads, 1) ln_gemm_kernel(const __grid_con
   uint64_t* a_empty = a_full + kLnASlots;                           // MMA commit
   uint64_t* acc_full = a_empty + kLnASlots;                         // [2] MMA commit
   uint64_t* acc_empty = acc_full + 2;                               // [2] 4 epilogue warps
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* raw_full = acc_empty + 2;                               // raw rows landed (tx)
+  uint64_t* raw_empty = raw_full + kLnRawStages;                    // a converter group
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(raw_empty + kLnRawStages);
   volatile uint32_t* abort = tslot + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -126,10 +135,17 @@ __global__ void __launch_bounds__(kLnThreads, 1) ln_gemm_kernel(const __grid_con
       mbar_init(&acc_full[h], 1);
       mbar_init(&acc_empty[h], 4);
     }
+    for (int s = 0; s < kLnRawStages; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tslot, 512);
-  if (threadIdx.x == 32) prefetch_tensormap(&xmap);
+  if (threadIdx.x == 32) {
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&qmap);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -204,6 +220,23 @@ __global__ void __launch_bounds__(kLnThreads, 1) ln_gemm_kernel(const __grid_con
       __syncwarp();
       for (int h = 0; h < nh; ++h) ++used[h];
     }
+  } else if (warp == 2) {
+    // ---------------- weight producer: the job's 128 rows of each K-block
+    int gkb = 0;
+    for (int i = 0;; ++i) {
+      const int u = job(i);
+      if (u < 0 || aborted()) break;
+      const int m0 = (u % a.MT) * kLnRows;
+      for (int kb = 0; kb < a.KB; ++kb, ++gkb) {
+        const int s = gkb % kLnRawStages;
+        ln_wait(&raw_empty[s], ((gkb / kLnRawStages) & 1) ^ 1, abort);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&raw_full[s], kLnRawBytes);
+          tma_load_2d(smem + kLnRaw + s * kLnRawBytes, &qmap, kLnKB * kb, m0, &raw_full[s]);
+        }
+        __syncwarp();
+      }
+    }
   } else if (warp < kLnEpi0) {
     // ---------------- converters: group g takes the CTA's K-blocks g, g + 2, ...
     const int w = warp - kLnConv0;
@@ -215,46 +248,39 @@ __global__ void __launch_bounds__(kLnThreads, 1) ln_gemm_kernel(const __grid_con
     int n_mine = 0;
     while (job(n_mine) >= 0) ++n_mine;
     const int total = n_mine * a.KB;
-    auto load_raw = [&](int gkb, uint4 (&v)[4]) {
-      if (gkb >= total) return;
-      const int i = gkb / a.KB, kb = gkb - i * a.KB;
-      const int u = job(i);
-      const int n = (u % a.MT) * kLnRows + r;
-      const int k0 = kLnKB * kb;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        v[c] = make_uint4(0u, 0u, 0u, 0u);
-        if (n < a.N && k0 + 16 * c < a.K)
-          v[c] = ldg_stream_v4(a.q + static_cast<int64_t>(n) * a.K + k0 + 16 * c);
-      }
-    };
-    uint4 cur[4], nxt[4];
-    load_raw(g, cur);
+    // this thread's raw row in a stage: 64-byte rows, 64-byte swizzle
+    const int raw_row = r * 64, swz = (r >> 1) & 3;
     int row_job = -1;
     float sc = 0.0f;
     for (int gkb = g; gkb < total; gkb += kLnGroups) {
-      load_raw(gkb + kLnGroups, nxt);
       const int i = gkb / a.KB;
       if (i != row_job) {   // the row scale of this job
         row_job = i;
         const int n = (job(i) % a.MT) * kLnRows + r;
         sc = n < a.N ? a.s[n] : 0.0f;
       }
+      const int sr = gkb % kLnRawStages;
+      ln_wait(&raw_full[sr], (gkb / kLnRawStages) & 1, abort);
+      const uint8_t* raw = smem + kLnRaw + sr * kLnRawBytes + raw_row;
+      uint4 rw[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) rw[c] = *reinterpret_cast<const uint4*>(raw + ((c ^ swz) << 4));
       uint32_t v[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) ln_convert16(cur[c], sc, v + 8 * c);
+      for (int c = 0; c < 4; ++c) ln_convert16(rw[c], sc, v + 8 * c);
       const int j = gkb % kLnASlots;
       ln_wait(&a_empty[j], ((gkb / kLnASlots) & 1) ^ 1, abort);
       tc_fence_after();
       tmem_st_x32(tmem + kLnTmemA + 32u * j + lane_base, v);
       tmem_st_wait();
       tc_fence_before();
+      // (no early exit anywhere in this loop: the group's named barrier needs
+      // all 128 threads; after a time-out every wait above returns at once)
       asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
-      if (w == 4 * g && lane == 0) mbar_arrive(&a_full[j]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
-      // (no early exit: the group's named barrier needs all 128 threads; after
-      // a time-out every wait above returns at once)
+      if (w == 4 * g && lane == 0) {
+        mbar_arrive(&a_full[j]);
+        mbar_arrive(&raw_empty[sr]);
+      }
     }
   } else {
     // ---------------- epilogue: warp reads TMEM lanes 32 (warp % 4) ..
@@ -327,6 +353,10 @@ extern "C" int qfn_linear_e4m3(const uint8_t* q, const float* s, const uint16_t*
   if ((rc = tensor_map_2d(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, T, K * 2, kLnKB, kLnTok,
                           CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &xmap)))
     return rc;
+  CUtensorMap qmap;
+  if ((rc = tensor_map_2d(q, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, kLnKB, kLnRows, CU_TENSOR_MAP_SWIZZLE_64B,
+                          dev->device, &qmap)))
+    return rc;
   static bool attr_set[64] = {};
   if (!attr_set[dev->device]) {
     cudaError_t e = cudaFuncSetAttribute(ln_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLnSmem);
@@ -356,7 +386,7 @@ extern "C" int qfn_linear_e4m3(const uint8_t* q, const float* s, const uint16_t*
   cfg.stream = as_stream(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, ln_gemm_kernel, xmap, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, ln_gemm_kernel, xmap, qmap, a);
   if (e != cudaSuccess) return set_error(QFN_ERR_CUDA, "ln_gemm launch: %s", cudaGetErrorString(e));
   return check_launch("ln_gemm_kernel");
 }
