@@ -13,26 +13,37 @@
 // time share the token tiles and walk the whole weight matrix through L2:
 //   warp 0       x producer: TMA boxes [256 tokens][64 k] (bf16, 128-byte
 //                swizzle) into a ring of kLnStages shared-memory stages;
-//   warp 1       MMA issuer: per K-block 4 k-steps x 2 accumulator halves
-//                (M = 128, N = 128 each; A from TMEM, B from shared memory);
+//   warp 1       MMA issuer: per K-block 4 k-steps of one M = 128, N = 256
+//                MMA (A from TMEM, B from shared memory).  The first kLnPre
+//                K-blocks of a job go into accumulator half 0 alone (N = 128)
+//                and then into half 1, so that the epilogue's reading of the
+//                previous job's half 1 overlaps them;
 //   warp 2       weight producer: TMA boxes [128 rows][64 B] of the e4m3
 //                bytes (64-byte swizzle) into a ring of kLnRawStages stages;
 //   warps 3-10   converters, two groups of four warps taking alternate
 //                K-blocks: thread = weight row; its 64 bytes of the K-block
 //                (four conflict-free 16-byte shared-memory reads) become
 //                bf16(fp32(q) * s) with the reference's two roundings and go
-//                into one of kLnASlots TMEM A slots;
+//                into one of kLnASlots TMEM A slots; a warp waits for a
+//                K-block's TMEM store only after converting its next one;
 //   warps 11-14  epilogue: TMEM -> RN bf16 -> y, each accumulator half
 //                released as soon as it has been read.
-// TMEM: columns [0, 256) the accumulator (two halves of 128 tokens),
-// [256, 512) eight A slots of 32 columns (one K-block of 64 bf16 each).
+// TMEM: columns [0, 256) the accumulator (tokens 0-127 and 128-255 of the
+// tile as halves), [256, 512) eight A slots of 32 columns (one K-block of 64
+// bf16 each).
 //
-// Why A in TMEM: from shared memory the A tiles would add 32 KB of shared
-// traffic per K-block (written by the converters, read by the MMAs) to the
-// x tile's 64 KB, in the 512 cycles the K-block's MMAs take.  The raw bytes
-// arrive by TMA: loaded by the converter threads themselves (a row per lane)
-// every warp load touched 32 L1 lines, and the converters stalled on them
-// (ncu: long-scoreboard 5.9 warps per issue, tensor pipe 40 % active).
+// Measured on B200 (T = 2048, the 12288 x 2560 and 2560 x 4096 shapes):
+//   - A in TMEM: from shared memory the A tiles would add 32 KB of shared
+//     traffic per K-block (written by the converters, read by the MMAs) to
+//     the x tile's 64 KB, in the 512 cycles the K-block's MMAs take;
+//   - one N = 256 MMA per k-step instead of an N = 128 MMA per half: the A
+//     tile is read from TMEM once, 190 -> 168 us for the two shapes;
+//   - raw bytes by TMA: loaded by the converter threads (a row per lane)
+//     every warp load touched 32 L1 lines and the converters stalled on them
+//     (320 -> 199 us);
+//   - tiles of 192 tokens with two accumulator buffers (no wait for the
+//     epilogue) measured slower for the large shape: 1,056 jobs take 8
+//     rounds of the 148 SMs and the conversion per FLOP grows by a third.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -48,9 +59,10 @@ constexpr int kLnRows = 128;                          // weight rows per job (MM
 constexpr int kLnTok = 256;                           // tokens per job: two accumulator halves
 constexpr int kLnHalf = 128;                          // tokens per half (MMA N)
 constexpr int kLnKB = 64;                             // k per K-block
-constexpr int kLnStages = 5;                          // x ring stages
-constexpr int kLnRawStages = 6;                       // raw weight ring stages
+constexpr int kLnStages = 6;                          // x ring stages
+constexpr int kLnRawStages = 4;                       // raw weight ring stages
 constexpr int kLnASlots = 8;                          // A slots in TMEM
+constexpr int kLnPre = 4;                             // K-blocks of a job issued into half 0 before half 1
 constexpr int kLnGroups = 2;                          // converter groups of four warps
 constexpr int kLnConv0 = 3;                           // first converter warp
 constexpr int kLnEpi0 = kLnConv0 + 4 * kLnGroups;     // first epilogue warp
@@ -128,7 +140,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       mbar_init(&ld_empty[s], 1);
     }
     for (int j = 0; j < kLnASlots; ++j) {
-      mbar_init(&a_full[j], 1);
+      mbar_init(&a_full[j], 4);
       mbar_init(&a_empty[j], 1);
     }
     for (int h = 0; h < 2; ++h) {
@@ -137,7 +149,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     }
     for (int s = 0; s < kLnRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 1);
+      mbar_init(&raw_empty[s], 4);
     }
     fence_mbar_init();
   }
@@ -184,6 +196,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer
     const uint32_t idesc = idesc_bf16(kLnRows, kLnHalf);
+    const uint32_t idesc2 = idesc_bf16(kLnRows, 2 * kLnHalf);
     const uint64_t bdesc0 = umma_desc_sw128(smem_u32(smem), 1024);
     uint32_t used[2] = {0u, 0u};
     int gkb = 0;
@@ -191,9 +204,39 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       const int u = job(i);
       if (u < 0 || aborted()) break;
       const int nh = halves(u);
-      for (int h = 0; h < nh; ++h) ln_wait(&acc_empty[h], (used[h] & 1) ^ 1, abort);
+      // the first kLnPre K-blocks into half 0 alone (N = 128), then into half 1
+      // once the epilogue has read it; then both halves in one N = 256 MMA
+      const int pre = nh == 2 ? min(kLnPre, a.KB) : 0;
+      ln_wait(&acc_empty[0], (used[0] & 1) ^ 1, abort);
       tc_fence_after();
-      for (int kb = 0; kb < a.KB; ++kb, ++gkb) {
+      for (int kb = 0; kb < pre; ++kb) {
+        const int g2 = gkb + kb, s = g2 % kLnStages, j = g2 % kLnASlots;
+        ln_wait(&ld_full[s], (g2 / kLnStages) & 1, abort);
+        ln_wait(&a_full[j], (g2 / kLnASlots) & 1, abort);
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t aslot = tmem + kLnTmemA + 32u * j;
+          const uint64_t bd = bdesc0 + ((s * kLnXBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_f16_ta(tmem, aslot + 8 * k, bd + 2u * k, idesc, (kb | k) != 0);
+        }
+        __syncwarp();
+      }
+      if (nh == 2) ln_wait(&acc_empty[1], (used[1] & 1) ^ 1, abort);
+      tc_fence_after();
+      for (int kb = 0; kb < pre; ++kb, ++gkb) {
+        const int s = gkb % kLnStages, j = gkb % kLnASlots;
+        if (elect_one()) {
+          const uint32_t aslot = tmem + kLnTmemA + 32u * j;
+          const uint64_t bd = bdesc0 + ((s * kLnXBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_f16_ta(tmem + kLnHalf, aslot + 8 * k, bd + (1024u + 2u * k), idesc, (kb | k) != 0);
+          mma_commit(&a_empty[j]);
+          mma_commit(&ld_empty[s]);
+        }
+        __syncwarp();
+      }
+      for (int kb = pre; kb < a.KB; ++kb, ++gkb) {
         const int s = gkb % kLnStages, j = gkb % kLnASlots;
         ln_wait(&ld_full[s], (gkb / kLnStages) & 1, abort);
         ln_wait(&a_full[j], (gkb / kLnASlots) & 1, abort);
@@ -202,13 +245,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
           const uint32_t aslot = tmem + kLnTmemA + 32u * j;
           const uint64_t bd = bdesc0 + ((s * kLnXBytes) >> 4);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              // half h: tokens 128h .. 128h + 127 of the tile = rows 128h.. of the x box (16 KB further)
-              if (h < nh) mma_f16_ta(tmem + kLnHalf * h, aslot + 8 * k, bd + (h * 1024u + 2u * k), idesc, (kb | k) != 0);
-            }
-          }
+          for (int k = 0; k < 4; ++k) mma_f16_ta(tmem, aslot + 8 * k, bd + 2u * k, nh == 2 ? idesc2 : idesc, (kb | k) != 0);
           mma_commit(&a_empty[j]);
           mma_commit(&ld_empty[s]);
         }
@@ -252,6 +289,13 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     const int raw_row = r * 64, swz = (r >> 1) & 3;
     int row_job = -1;
     float sc = 0.0f;
+    int pend = -1;   // K-block whose TMEM store is in flight
+    auto signal = [&](int gk) {   // that store has landed: its A slot is full (one arrival per warp)
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[gk % kLnASlots]);
+    };
     for (int gkb = g; gkb < total; gkb += kLnGroups) {
       const int i = gkb / a.KB;
       if (i != row_job) {   // the row scale of this job
@@ -268,20 +312,16 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       uint32_t v[32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) ln_convert16(rw[c], sc, v + 8 * c);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[sr]);
+      if (pend >= 0) signal(pend);
       const int j = gkb % kLnASlots;
       ln_wait(&a_empty[j], ((gkb / kLnASlots) & 1) ^ 1, abort);
       tc_fence_after();
       tmem_st_x32(tmem + kLnTmemA + 32u * j + lane_base, v);
-      tmem_st_wait();
-      tc_fence_before();
-      // (no early exit anywhere in this loop: the group's named barrier needs
-      // all 128 threads; after a time-out every wait above returns at once)
-      asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory");
-      if (w == 4 * g && lane == 0) {
-        mbar_arrive(&a_full[j]);
-        mbar_arrive(&raw_empty[sr]);
-      }
+      pend = gkb;
     }
+    if (pend >= 0) signal(pend);
   } else {
     // ---------------- epilogue: warp reads TMEM lanes 32 (warp % 4) ..
     const int quarter = warp & 3;
