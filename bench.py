@@ -26,11 +26,13 @@ grouped SwiGLU expert GEMM and the weighted combine (qmoe.moe_prefill).
 
 Sub-records in the same line (same process, same expert table): at N = 1 the
 bs=1 decode layer over the 48-layer stack (config 2, the first half of the
-BASELINE metric), the FP8 GEMV (config 1) and batched decode (config 4); at
-N > 1 batched decode expert-parallel (config 4).  Each carries its own
-roofline, e2e, parity and (N = 1) CPU baseline.
+BASELINE metric), the FP8 GEMV (config 1), the decode MoE block, the delta
+rule, the FP8 linear layer for T > 1 (config-1 weight shapes, 2,048 tokens)
+and batched decode (config 4); at N > 1 batched decode expert-parallel
+(config 4).  Each carries its own roofline, e2e and parity.
 
-`--workload decode|gemv|batch-decode|fp8-linear` prints one of those alone.
+`--workload decode|gemv|batch-decode|fp8-linear|decode-block|deltanet` prints
+one of those alone.
 `--impl reference` times the reference's CPU path (the C restatement in
 oracle/) on this host's cores on a bounded sample of the same workload.
 """
