@@ -8,7 +8,9 @@
 // K-block from the e4m3 bytes straight into TMEM, where they are the A
 // operand of tcgen05.mma kind::f16 (bf16 x bf16 -> fp32).
 //
-// Job = (128 weight rows, 256 tokens), dealt to the CTAs (one per SM, 480
+// Job = (128 weight rows, tn tokens: 256, or fewer when that fills the SMs'
+// rounds better; 160 for the 2560 x 4096 shape at 2,048 tokens, 54.7 -> 52.4
+// us), dealt to the CTAs (one per SM, 480
 // threads) in the order row tile fastest, so that the CTAs running at one
 // time share the token tiles and walk the whole weight matrix through L2:
 //   warp 0       x producer: TMA boxes [256 tokens][64 k] (bf16, 128-byte
@@ -56,8 +58,7 @@
 namespace qfn {
 
 constexpr int kLnRows = 128;                          // weight rows per job (MMA M)
-constexpr int kLnTok = 256;                           // tokens per job: two accumulator halves
-constexpr int kLnHalf = 128;                          // tokens per half (MMA N)
+constexpr int kLnTok = 256;                           // most tokens per job (two accumulator halves)
 constexpr int kLnKB = 64;                             // k per K-block
 constexpr int kLnStages = 6;                          // x ring stages
 constexpr int kLnRawStages = 4;                       // raw weight ring stages
@@ -98,6 +99,7 @@ struct LnArgs {
   int T, N, K;
   int KB;             // K-blocks per job
   int MT;             // row tiles
+  int tn, hn;         // tokens per job (a multiple of 32, <= 256) and per accumulator half (tn / 2)
   int n_jobs;
 };
 
@@ -174,7 +176,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
   // a time-out seen by any lane of the warp (warp-uniform, for loop exits)
   auto aborted = [&]() -> bool { return __any_sync(0xffffffffu, *abort != 0u); };
   // accumulator halves a job uses (1 when its token tile holds <= 128 tokens)
-  auto halves = [&](int u) -> int { return a.T - (u / a.MT) * kLnTok > kLnHalf ? 2 : 1; };
+  auto halves = [&](int u) -> int { return a.T - (u / a.MT) * a.tn > a.hn ? 2 : 1; };
 
   if (warp == 0) {
     // ---------------- x producer
@@ -182,12 +184,12 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     for (int i = 0;; ++i) {
       const int u = job(i);
       if (u < 0 || aborted()) break;
-      const int t0 = (u / a.MT) * kLnTok;
+      const int t0 = (u / a.MT) * a.tn;
       for (int kb = 0; kb < a.KB; ++kb, ++gkb) {
         const int s = gkb % kLnStages;
         ln_wait(&ld_empty[s], ((gkb / kLnStages) & 1) ^ 1, abort);
         if (elect_one()) {
-          mbar_arrive_expect_tx(&ld_full[s], kLnXBytes);
+          mbar_arrive_expect_tx(&ld_full[s], static_cast<uint32_t>(a.tn) * kLnKB * 2);
           tma_load_2d(smem + s * kLnXBytes, &xmap, kLnKB * kb, t0, &ld_full[s]);
         }
         __syncwarp();
@@ -195,8 +197,10 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
-    const uint32_t idesc = idesc_bf16(kLnRows, kLnHalf);
-    const uint32_t idesc2 = idesc_bf16(kLnRows, 2 * kLnHalf);
+    const uint32_t idesc = idesc_bf16(kLnRows, a.hn);        // one half
+    const uint32_t idesc2 = idesc_bf16(kLnRows, 2 * a.hn);   // both halves (the tile)
+    const uint32_t hcol = static_cast<uint32_t>(a.hn);           // half 1's first accumulator column
+    const uint32_t hrow = static_cast<uint32_t>(a.hn) * 8u;      // its first x row in the stage, in 16-byte units
     const uint64_t bdesc0 = umma_desc_sw128(smem_u32(smem), 1024);
     uint32_t used[2] = {0u, 0u};
     int gkb = 0;
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
           const uint32_t aslot = tmem + kLnTmemA + 32u * j;
           const uint64_t bd = bdesc0 + ((s * kLnXBytes) >> 4);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) mma_f16_ta(tmem + kLnHalf, aslot + 8 * k, bd + (1024u + 2u * k), idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k) mma_f16_ta(tmem + hcol, aslot + 8 * k, bd + (hrow + 2u * k), idesc, (kb | k) != 0);
           mma_commit(&a_empty[j]);
           mma_commit(&ld_empty[s]);
         }
@@ -331,15 +335,15 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       if (u < 0 || aborted()) break;
       const int nh = halves(u);
       const int n = (u % a.MT) * kLnRows + 32 * quarter + lane;
-      const int t0 = (u / a.MT) * kLnTok;
+      const int t0 = (u / a.MT) * a.tn;
       for (int h = 0; h < nh; ++h) {
         ln_wait(&acc_full[h], used[h] & 1, abort);
         tc_fence_after();
-        const int cols = min(kLnHalf, a.T - t0 - kLnHalf * h);
-        uint16_t* yc = a.y + static_cast<int64_t>(t0 + kLnHalf * h) * a.N + n;
+        const int cols = min(a.hn, a.T - t0 - a.hn * h);
+        uint16_t* yc = a.y + static_cast<int64_t>(t0 + a.hn * h) * a.N + n;
         for (int c0 = 0; c0 < cols; c0 += 16) {
           uint32_t v[16];
-          tmem_ld_x16(tmem + (static_cast<uint32_t>(32 * quarter) << 16) + kLnHalf * h + c0, v);
+          tmem_ld_x16(tmem + (static_cast<uint32_t>(32 * quarter) << 16) + a.hn * h + c0, v);
           if (n < a.N) {
             const int lim = cols - c0;
             uint16_t* p = yc + static_cast<int64_t>(c0) * a.N;
@@ -390,7 +394,20 @@ extern "C" int qfn_linear_e4m3(const uint8_t* q, const float* s, const uint16_t*
   int rc = current_device(&dev);
   if (rc) return rc;
   CUtensorMap xmap;
-  if ((rc = tensor_map_2d(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, T, K * 2, kLnKB, kLnTok,
+  // tokens per job: the tile (256 down to 128, a multiple of 32) whose jobs fill the
+  // SMs' rounds best, each job also paying a fixed cost of about 32 tokens'
+  // worth of MMAs (pipeline fill, epilogue)
+  const int64_t MT = (N + kLnRows - 1) / kLnRows;
+  int tn = kLnTok;
+  int64_t best = -1;
+  for (int c = kLnTok; c >= 128; c -= 32) {
+    const int64_t rounds = (MT * ((T + c - 1) / c) + dev->sm_count - 1) / dev->sm_count;
+    if (best < 0 || rounds * (c + 32) < best) {
+      best = rounds * (c + 32);
+      tn = c;
+    }
+  }
+  if ((rc = tensor_map_2d(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, T, K * 2, kLnKB, static_cast<uint32_t>(tn),
                           CU_TENSOR_MAP_SWIZZLE_128B, dev->device, &xmap)))
     return rc;
   CUtensorMap qmap;
@@ -412,7 +429,9 @@ extern "C" int qfn_linear_e4m3(const uint8_t* q, const float* s, const uint16_t*
   a.K = static_cast<int>(K);
   a.KB = static_cast<int>((K + kLnKB - 1) / kLnKB);
   a.MT = static_cast<int>((N + kLnRows - 1) / kLnRows);
-  const int64_t jobs = static_cast<int64_t>(a.MT) * ((T + kLnTok - 1) / kLnTok);
+  a.tn = tn;
+  a.hn = tn / 2;
+  const int64_t jobs = MT * ((T + tn - 1) / tn);
   QFN_REQUIRE(jobs < (int64_t(1) << 30), QFN_ERR_UNSUPPORTED, "qfn_linear_e4m3: too many tiles");
   a.n_jobs = static_cast<int>(jobs);
   const unsigned grid = static_cast<unsigned>(jobs < dev->sm_count ? jobs : dev->sm_count);
