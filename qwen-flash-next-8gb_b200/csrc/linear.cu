@@ -13,11 +13,11 @@
 // us), dealt to the CTAs (one per SM, 480
 // threads) in the order row tile fastest, so that the CTAs running at one
 // time share the token tiles and walk the whole weight matrix through L2:
-//   warp 0       x producer: TMA boxes [256 tokens][64 k] (bf16, 128-byte
+//   warp 0       x producer: TMA boxes [tn tokens][64 k] (bf16, 128-byte
 //                swizzle) into a ring of kLnStages shared-memory stages;
-//   warp 1       MMA issuer: per K-block 4 k-steps of one M = 128, N = 256
+//   warp 1       MMA issuer: per K-block 4 k-steps of one M = 128, N = tn
 //                MMA (A from TMEM, B from shared memory).  The first kLnPre
-//                K-blocks of a job go into accumulator half 0 alone (N = 128)
+//                K-blocks of a job go into accumulator half 0 alone (N = tn / 2)
 //                and then into half 1, so that the epilogue's reading of the
 //                previous job's half 1 overlaps them;
 //   warp 2       weight producer: TMA boxes [128 rows][64 B] of the e4m3
@@ -30,8 +30,8 @@
 //                K-block's TMEM store only after converting its next one;
 //   warps 11-14  epilogue: TMEM -> RN bf16 -> y, each accumulator half
 //                released as soon as it has been read.
-// TMEM: columns [0, 256) the accumulator (tokens 0-127 and 128-255 of the
-// tile as halves), [256, 512) eight A slots of 32 columns (one K-block of 64
+// TMEM: columns [0, tn) the accumulator (the tile's first and second tn / 2
+// tokens as halves), [256, 512) eight A slots of 32 columns (one K-block of 64
 // bf16 each).
 //
 // Measured on B200 (T = 2048, the 12288 x 2560 and 2560 x 4096 shapes):
