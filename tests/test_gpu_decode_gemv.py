@@ -299,7 +299,7 @@ def _bf16_steps_off(y, exact):
 
 
 @pytest.mark.parametrize("T,N,K", [(1, 2560, 4096), (2, 2560, 4096), (17, 2560, 4096), (256, 2560, 4096),
-                                   (300, 333, 1040), (129, 128, 16), (1000, 12288, 2560)])
+                                   (300, 333, 1040), (129, 128, 16), (3, 1, 32), (1000, 12288, 2560)])
 def test_fp8_linear_matches_reference(T, N, K):
     """Lin.__call__ (qwen_engine.py:79-83) for T tokens.  T > 1: the tcgen05
     GEMM against the exact products of the reference's bf16 weights
@@ -329,6 +329,26 @@ def test_fp8_linear_matches_reference(T, N, K):
     exact = x[rows].double().numpy() @ w.T
     assert _bf16_steps_off(got, exact).max() <= 1.0
     assert (got != oracle.bf16_round(exact.astype(np.float32))).mean() < 0.01
+
+
+def test_fp8_linear_nan_weight_codes():
+    """An e4m3 NaN code (S.1111.111) in a weight row makes that output column
+    NaN for every token, as F.linear on the reference's bf16 weights does; the
+    other columns are unaffected."""
+    N, K, T = 256, 512, 40
+    q, s, _ = gemv_inputs(N, K, 31, 32)
+    q = q.copy()
+    q[3, 100] = 0x7F
+    q[200, 7] = 0xFF
+    x = torch.randn(T, K, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    qd, sd, xd = cuda(q).view(torch.float8_e4m3fn), cuda(s)[:, None], x.to(DEV)
+    y = fp8gemv.linear(xd, qd, sd).float().cpu()
+    ref = torch.nn.functional.linear(xd, (qd.to(torch.bfloat16) * sd).to(torch.bfloat16)).float().cpu()
+    nan = torch.isnan(ref)
+    assert nan[:, 3].all() and nan[:, 200].all() and nan.sum() == 2 * T
+    assert torch.equal(torch.isnan(y), nan)
+    ok = ~nan
+    assert (y[ok] - ref[ok]).abs().max().item() <= 2.0 ** -7 * ref[ok].abs().max().item()
 
 
 def test_fp8_linear_repeated_calls_and_graph():
