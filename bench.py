@@ -990,7 +990,7 @@ def batch_decode_record(ctx, steps):
     return rec
 
 
-# ---------------------------------------------------------------- the decode MoE block
+# ---------------------------------------------------------------- the decode MoE block (router + routed + shared expert)
 SH_INTER = 640      # shared-expert width: the checkpoint's config.json is absent here; the routed experts' 640 assumed
 BLOCK_METRIC = "decode MoE block us/layer (router + 10 routed NVFP4 experts + bf16 shared expert, 48 layers)"
 

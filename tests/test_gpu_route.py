@@ -1,4 +1,4 @@
-"""GPU parity of the decode MoE block's prologue and epilogue:
+"""GPU parity of the decode MoE block's prologue and epilogue (router, shared expert):
 the fused router (routing.route_fused, the C ABI's qfn_moe_route), the bf16
 shared expert with the combine (moe_block.shared_expert, qfn_shared_expert)
 and the whole device-side block (moe_block.DecodeMoE) against the CPU oracle.
